@@ -1,0 +1,129 @@
+"""Generate golden vectors by importing the UNMODIFIED reference LVSA package.
+
+Run in a container where the reference checkout exists:
+
+    python tests/golden/make_golden.py /path/to/LongVideoSparseAttention
+
+It writes ``patterns.npz`` (frame-level ``LVSAMetadata.build`` outputs) and
+``attn_*.npz`` (seeded bf16-representable inputs with the reference's fp32
+``lvsa_sdpa`` output and dense text-query rows).  The fixtures are committed;
+the tests never need the reference at run time.
+"""
+
+import json
+import os
+import sys
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+# (name, T, P, W, n_first, kfi, offset, expand, rank, world)
+PATTERN_CASES = [
+    ("cfg1", 9, 1560, 1, 1, 4, 3, True, 0, 1),
+    ("cfg2", 81, 1560, 2, 1, 4, 0, True, 0, 1),
+    ("cfg3_s0", 121, 1560, 2, 1, 4, 0, True, 0, 1),
+    ("cfg3_s1", 121, 1560, 2, 1, 4, 1, True, 0, 1),
+    ("cfg3_s2", 121, 1560, 2, 1, 4, 2, True, 0, 1),
+    ("cfg3_s3", 121, 1560, 2, 1, 4, 3, True, 0, 1),
+    ("cfg4", 49, 1590, 2, 1, 4, 0, True, 0, 1),
+    ("cfg5", 49, 1350, 1, 1, 3, 0, True, 0, 1),
+    ("w0", 21, 16, 0, 1, 5, 0, True, 0, 1),
+    ("noexpand", 21, 16, 3, 1, 5, 2, False, 0, 1),
+    ("kfi_none", 17, 8, 2, 4, None, 0, True, 0, 1),
+    ("t1", 1, 8, 1, 1, 4, 0, True, 0, 1),
+    ("small_T", 5, 4, 3, 1, 2, 1, True, 0, 1),
+    ("nfirst3", 33, 12, 2, 3, 7, 5, True, 0, 1),
+    ("big_off", 30, 6, 2, 1, 4, 11, True, 0, 1),
+    ("wide_w", 40, 10, 9, 2, 6, 4, True, 0, 1),
+    ("kfi1", 12, 8, 1, 1, 1, 0, True, 0, 1),
+    ("cp_r0", 20, 10, 2, 1, 5, 0, True, 0, 2),
+    ("cp_r1", 20, 10, 2, 1, 5, 0, True, 1, 2),
+    ("cp_r2of4", 21, 8, 1, 1, 4, 2, True, 2, 4),
+]
+
+# (name, T, P, H, Hkv, D, W, n_first, kfi, offset, n_text, B, seed)
+ATTN_CASES = [
+    ("a_small", 9, 8, 2, 2, 64, 1, 1, 4, 3, 0, 1, 1),
+    ("a_text", 7, 12, 2, 2, 128, 1, 1, 3, 1, 10, 1, 2),
+    ("a_gqa", 6, 16, 4, 2, 64, 1, 1, 2, 0, 5, 2, 3),
+    ("a_w0", 8, 10, 2, 2, 64, 0, 1, 3, 2, 0, 1, 4),
+    ("a_p130", 5, 130, 2, 2, 128, 1, 1, 2, 1, 0, 1, 5),
+    ("a_t1", 1, 20, 2, 2, 64, 1, 1, 4, 0, 3, 1, 6),
+    ("a_d128", 10, 40, 3, 3, 128, 2, 1, 4, 2, 17, 1, 7),
+]
+
+
+def bf16_round(x: torch.Tensor) -> torch.Tensor:
+    return x.to(torch.bfloat16).to(torch.float32)
+
+
+def main(ref_root: str) -> None:
+    sys.path.insert(0, ref_root)
+    from lvsa.sparse_attention import LVSAMetadata, lvsa_sdpa, compute_boundary_guard_frames
+    from lvsa.lvsa_processor import DistributedLVSAProcessor
+
+    pats = {}
+    meta_json = {}
+    for name, T, P, W, nf, kfi, off, exp, rank, world in PATTERN_CASES:
+        guards = (compute_boundary_guard_frames(T, T * P // world, P, world, W)
+                  if world > 1 else None)
+        m = LVSAMetadata.build(total_latent_frames=T, num_patches=P, window_size=W,
+                               n_first_frames=nf, key_frame_interval=kfi, rank=rank,
+                               world=world, expand_window=exp, keyframe_offset=off,
+                               boundary_guards=guards)
+        pats[f"{name}.global_indices"] = np.asarray(m.global_indices, dtype=np.int32)
+        pats[f"{name}.global_frame_mask"] = m.global_frame_mask.numpy()
+        pats[f"{name}.window_bounds"] = m.window_bounds.numpy()
+        pats[f"{name}.attended_indices"] = m.attended_indices.numpy()
+        pats[f"{name}.fi_indptr"] = m.fi_indptr.numpy()
+        pats[f"{name}.fi_indices"] = m.fi_indices.numpy()
+        pats[f"{name}.local_frames"] = np.asarray(m.local_frames, dtype=np.int64)
+        wc = [(f, s, e) for f, parts in sorted(m.window_ctx.items()) for s, e in parts]
+        pats[f"{name}.window_ctx"] = np.asarray(wc, dtype=np.int64).reshape(-1, 3)
+        meta_json[name] = dict(T=T, P=P, W=W, n_first=nf, kfi=kfi, offset=off, expand=exp,
+                               rank=rank, world=world, guards=guards or [],
+                               local_seq=m.local_seq, fi_MB=m.fi_MB,
+                               fi_compact_n=m.fi_compact_n, attended_C=m.attended_C)
+    np.savez_compressed(os.path.join(HERE, "patterns.npz"), **pats)
+    with open(os.path.join(HERE, "patterns.json"), "w") as fh:
+        json.dump(meta_json, fh, indent=1, sort_keys=True)
+
+    for name, T, P, H, Hkv, D, W, nf, kfi, off, nt, B, seed in ATTN_CASES:
+        g = torch.Generator().manual_seed(seed)
+        N = T * P
+        q = bf16_round(torch.randn(B, N, H, D, generator=g))
+        k = bf16_round(torch.randn(B, N, Hkv, D, generator=g))
+        v = bf16_round(torch.randn(B, N, Hkv, D, generator=g))
+        tq = bf16_round(torch.randn(B, nt, H, D, generator=g))
+        tk = bf16_round(torch.randn(B, nt, Hkv, D, generator=g))
+        tv = bf16_round(torch.randn(B, nt, Hkv, D, generator=g))
+        m = LVSAMetadata.build(total_latent_frames=T, num_patches=P, window_size=W,
+                               n_first_frames=nf, key_frame_interval=kfi, rank=0, world=1,
+                               expand_window=True, keyframe_offset=off)
+        # global K/V as lvsa_processor._build_global_kv (world=1) + text appended (:545-549)
+        gi = torch.tensor(m.global_indices, dtype=torch.long)
+        idx = (gi[:, None] * P + torch.arange(P)[None, :]).flatten()
+        kg = torch.cat([k[:, idx], tk], dim=1)
+        vg = torch.cat([v[:, idx], tv], dim=1)
+        out = lvsa_sdpa(q, k, v, kg, vg, m)
+        arrays = dict(q=q.numpy(), k=k.numpy(), v=v.numpy(), out=out.numpy(),
+                      text_q=tq.numpy(), text_k=tk.numpy(), text_v=tv.numpy())
+        if nt > 0:
+            if Hkv != H:
+                rep = H // Hkv
+                fk = torch.cat([k, tk], 1).repeat_interleave(rep, dim=2)
+                fv = torch.cat([v, tv], 1).repeat_interleave(rep, dim=2)
+            else:
+                fk, fv = torch.cat([k, tk], 1), torch.cat([v, tv], 1)
+            arrays["text_out"] = DistributedLVSAProcessor._compute_full_attention(
+                None, tq, fk, fv).numpy()
+        arrays["params"] = np.asarray([T, P, H, Hkv, D, W, nf, kfi, off, nt, B, seed],
+                                      dtype=np.int64)
+        np.savez_compressed(os.path.join(HERE, f"attn_{name}.npz"), **arrays)
+        print("wrote", name)
+
+
+if __name__ == "__main__":
+    main(sys.argv[1] if len(sys.argv) > 1 else os.environ.get("LVSA_REFERENCE_ROOT", "."))
