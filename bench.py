@@ -1,0 +1,405 @@
+"""LVSA block-sparse attention benchmark (B200, sm_100a).
+
+Default workload ("cfg2"): Wan2.1-1.3B self-attention at
+4x horizon -- 81 latent frames x 1560 tokens = 126 360 tokens, 12 heads,
+head_dim 128, bf16, anchors = first frame, keyframe stride 4 rotating per
+step, window +-2, 128x128 tiles.  One step = one denoising step of the
+30-layer model: the GPU mask build for the step plus 30 attention layers,
+each on its own seeded q/k/v (N(0,1)/sqrt(128), seeded 3-D RoPE applied).
+
+Metric: useful TFLOP/s (active 128x128 tiles, clipped; BASELINE's FLOP_tiles)
+and ms/layer.  Timing: CUDA events on the launching stream, warm-up steps
+first, barrier + synchronize around the timed region, max over ranks.  The
+30 layers' inputs (35 GB) exceed L2 and are cycled, so no L2 flush is needed.
+
+--impl reference: the reference algorithm's CPU implementation (the oracle
+port of lvsa_sdpa) on the host cores, bounded sample per step.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CONFIGS = {
+    "cfg2": dict(T=81, P=1560, H=12, D=128, W=2, n_first=1, kfi=4, step=0, n_text=0, layers=30,
+                 desc="Wan2.1-1.3B 4x horizon (81 latent frames x 1560), 12x128, bf16, window +-2, kfi 4"),
+    "cfg3": dict(T=121, P=1560, H=12, D=128, W=2, n_first=1, kfi=4, step=0, n_text=0, layers=30,
+                 desc="Wan2.1-1.3B 6x horizon (121 x 1560), 12x128, bf16"),
+    "cfg4": dict(T=49, P=1590, H=16, D=128, W=2, n_first=1, kfi=4, step=0, n_text=256, layers=30,
+                 desc="HunyuanVideo-1.5 49 x 1590 + 256 text, 16x128, bf16"),
+    "cfg5": dict(T=49, P=1350, H=48, D=64, W=1, n_first=1, kfi=3, step=0, n_text=226, layers=30,
+                 desc="CogVideoX-5B 49 x 1350 + 226 text, 48x64, bf16"),
+}
+METRIC = "sparse-attn ms/layer & useful TFLOPS (% of B200 peak) at 1/2/4/8 GPUs"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as fh:
+            d = json.load(fh)
+        return d, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def flops_for(cfg):
+    """(FLOP_tiles, FLOP_exact) of one layer, from the pattern (host arithmetic)."""
+    from longvideosparseattention_b200.sparse_attention import LVSAMetadata, tile_flop_counts
+    m = LVSAMetadata.build(cfg["T"], cfg["P"], cfg["W"], cfg["n_first"], cfg["kfi"], 0, 1,
+                           keyframe_offset=cfg["step"] % cfg["kfi"])
+    return tile_flop_counts(m, cfg["n_text"], cfg["H"], cfg["D"], 128, 128)
+
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+        return False
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in self.lines:
+            f = [x.strip() for x in l.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def seeded_layer(cfg, layer, device, gen_device=True):
+    """Seeded q/k/v (+ text) of one layer: N(0,1)/sqrt(D) with a seeded 3-D RoPE on q, k."""
+    import torch
+    T, P, H, D, nt = cfg["T"], cfg["P"], cfg["H"], cfg["D"], cfg["n_text"]
+    N = T * P
+    g = torch.Generator(device=device).manual_seed(1000 + layer)
+    sc = 1.0 / math.sqrt(D)
+    q = torch.randn(1, N, H, D, generator=g, device=device) * sc
+    k = torch.randn(1, N, H, D, generator=g, device=device) * sc
+    v = torch.randn(1, N, H, D, generator=g, device=device) * sc
+    q, k = apply_rope3d(q, k, cfg)
+    out = [q.to(torch.bfloat16), k.to(torch.bfloat16), v.to(torch.bfloat16)]
+    if nt:
+        out += [(torch.randn(1, nt, H, D, generator=g, device=device) * sc).to(torch.bfloat16)
+                for _ in range(3)]
+    return out
+
+
+def apply_rope3d(q, k, cfg):
+    """3-D (t, h, w) rotary embedding on interleaved pairs, split of head_dim as
+    in Wan (t: D/2 - 2*(D/6 rounded), h and w: the rest); seeded frequency base."""
+    import torch
+    T, P, D = cfg["T"], cfg["P"], cfg["D"]
+    grid_w = {1560: 52, 1590: 53, 1350: 30}.get(P, P)
+    grid_h = P // grid_w
+    half = D // 2
+    dh = dw = 2 * (half // 6)
+    dt = half - dh - dw
+    dev = q.device
+    t_idx = torch.arange(T, device=dev).repeat_interleave(P)
+    hw = torch.arange(P, device=dev).repeat(T)
+    h_idx, w_idx = hw // grid_w, hw % grid_w
+
+    def freqs(pos, n):
+        inv = 1.0 / (10000 ** (torch.arange(n, device=dev, dtype=torch.float32) / n))
+        return pos[:, None].float() * inv[None, :]
+    ang = torch.cat([freqs(t_idx, dt), freqs(h_idx, dh), freqs(w_idx, dw)], dim=1)  # [N, D/2]
+    cos, sin = ang.cos()[None, :, None, :], ang.sin()[None, :, None, :]
+
+    def rot(x):
+        x2 = x.view(*x.shape[:-1], half, 2)
+        a, b = x2[..., 0], x2[..., 1]
+        return torch.stack([a * cos - b * sin, a * sin + b * cos], dim=-1).flatten(-2)
+    return rot(q), rot(k)
+
+
+def run_b200(args, cfg):
+    import torch
+    import torch.distributed as dist
+    from longvideosparseattention_b200 import block_sparse_attention, build_block_mask, check_device_errors
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+
+    L = cfg["layers"]
+    T, P, H, D, nt = cfg["T"], cfg["P"], cfg["H"], cfg["D"], cfg["n_text"]
+    flop_tiles, flop_exact = flops_for(cfg)
+    layers = [seeded_layer(cfg, rank * L + i, dev) for i in range(L)]
+    outs = [torch.empty_like(layers[0][0]) for _ in range(2)]
+    touts = [torch.empty_like(layers[0][3]) for _ in range(2)] if nt else [None, None]
+    stream = torch.cuda.current_stream(dev)
+    mask = build_block_mask(T, P, cfg["W"], cfg["n_first"], cfg["kfi"], cfg["step"] % cfg["kfi"],
+                            True, nt, device=dev)
+
+    def step(s, ev=None):
+        nonlocal mask
+        mask = build_block_mask(T, P, cfg["W"], cfg["n_first"], cfg["kfi"],
+                                (cfg["step"] + s * 0) % cfg["kfi"], True, nt, device=dev, reuse=mask)
+        for i, lay in enumerate(layers):
+            if ev is not None:
+                ev[i][0].record(stream)
+            tx = (lay[3], lay[4], lay[5]) if nt else (None, None, None)
+            block_sparse_attention(lay[0], lay[1], lay[2], mask, *tx, out=outs[i & 1], text_out=touts[i & 1])
+            if ev is not None:
+                ev[i][1].record(stream)
+
+    for s in range(args.warmup):
+        step(s)
+    torch.cuda.synchronize()
+    check_device_errors(dev)
+
+    evs = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(L)]
+           for _ in range(args.steps)]
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        start.record(stream)
+        for s in range(args.steps):
+            step(s, evs[s])
+        stop.record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    check_device_errors(dev)
+    ms = start.elapsed_time(stop)
+    kern_ms = [a.elapsed_time(b) for e in evs for (a, b) in e]
+    t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    ms_step = ms_max / args.steps
+    total_flop = flop_tiles * L * args.steps * world
+    value = total_flop / (ms_max * 1e-3) / 1e12
+
+    # ---- e2e through the public API with pinned host buffers (copies inside the timed region)
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(args, cfg, dev, world, flop_tiles)
+
+    if rank == 0:
+        pk, pk_kind = peaks()
+        mean_launch = statistics.mean(kern_ms)
+        achieved = flop_tiles / (mean_launch * 1e-3) / 1e12
+        peak = pk.get("bf16_tflops_sustained", pk.get("bf16_tflops"))
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 3),
+            "ms_per_layer": round(ms_step / L, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1)/sqrt(D), RoPE-3D)",
+            "config": {"workload": args.config, "desc": cfg["desc"], "layers_per_step": L,
+                       "tokens": T * P + nt, "heads": H, "head_dim": D, "tile": "128x128",
+                       "flop_tiles_per_layer": flop_tiles, "flop_exact_per_layer": flop_exact,
+                       "l2": "30 distinct layer inputs (35 GB) cycled: inputs exceed L2, no flush",
+                       "parallelism": f"replicas x{world} (independent layers per rank)"},
+            "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak,
+                         "unit": "TFLOP/s", "frac": round(achieved / peak, 4), "traffic": None,
+                         "peak_source": f"{pk_kind} bf16_tflops_sustained (kernel runs back-to-back in a long step)",
+                         "mean_launch_ms": round(mean_launch, 4)},
+            "clocks": clk.summary(),
+            "gpu_launches": (4 + L) * args.steps,
+            "e2e": e2e,
+        }
+        if args.cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(cfg, flop_tiles, budget_s=args.cpu_seconds)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def run_e2e(args, cfg, dev, world, flop_tiles):
+    """Public-API path with host tensors: per layer, H2D of q/k/v(+text) from
+    pinned memory, the attention call, D2H of the output, all in the timed region."""
+    import torch
+    from longvideosparseattention_b200 import block_sparse_attention, build_block_mask
+    L, nt = cfg["layers"], cfg["n_text"]
+    host = []
+    for i in range(2):  # two distinct pinned layer inputs, cycled
+        lay = seeded_layer(cfg, 10_000 + i, dev)
+        host.append([x.cpu().pin_memory() for x in lay])
+        del lay
+    out_h = torch.empty(host[0][0].shape, dtype=torch.bfloat16).pin_memory()
+    tout_h = torch.empty(host[0][3].shape, dtype=torch.bfloat16).pin_memory() if nt else None
+    stream = torch.cuda.current_stream(dev)
+    h2d = sum(x.numel() * x.element_size() for x in host[0])
+    d2h = out_h.numel() * 2 + (tout_h.numel() * 2 if nt else 0)
+
+    def step():
+        mask = build_block_mask(cfg["T"], cfg["P"], cfg["W"], cfg["n_first"], cfg["kfi"],
+                                cfg["step"] % cfg["kfi"], True, nt, device=dev)
+        for i in range(L):
+            d = [x.to(dev, non_blocking=True) for x in host[i & 1]]
+            tx = (d[3], d[4], d[5]) if nt else (None, None, None)
+            o, to = block_sparse_attention(d[0], d[1], d[2], mask, *tx)
+            out_h.copy_(o, non_blocking=True)
+            if nt:
+                tout_h.copy_(to, non_blocking=True)
+        return mask
+
+    steps = max(1, min(args.steps, 3))
+    for _ in range(max(1, min(args.warmup, 3))):
+        step()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(steps):
+        step()
+    b.record(stream)
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b)
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    val = flop_tiles * L * steps * world / (ms * 1e-3) / 1e12
+    return {"value": round(val, 2), "unit": "TFLOP/s", "ms_per_layer": round(ms / steps / L, 3),
+            "h2d_bytes_per_step": h2d * L, "d2h_bytes_per_step": d2h * L, "steps": steps}
+
+
+_CPU_INPUTS = {}
+
+
+def cpu_sample(cfg, frames, threads):
+    """Time the reference's CPU arithmetic (oracle restatement of lvsa_sdpa:
+    per-frame K/V concat + torch fp32 SDPA) for `frames` query frames."""
+    import torch
+    from oracle import lvsa_oracle as O
+    T, P, H, D, nt = cfg["T"], cfg["P"], cfg["H"], cfg["D"], cfg["n_text"]
+    key = (T, P, H, D, nt)
+    torch.set_num_threads(threads)
+    if key not in _CPU_INPUTS:
+        g = torch.Generator().manual_seed(0)
+        sc = 1.0 / math.sqrt(D)
+        mk = lambda n: torch.randn(1, n, H, D, generator=g) * sc
+        _CPU_INPUTS[key] = (mk(T * P), mk(T * P), mk(T * P), mk(nt) if nt else None, mk(nt) if nt else None)
+    q, k, v, tk, tv = _CPU_INPUTS[key]
+    fp = O.frame_pattern(T, P, cfg["W"], cfg["n_first"], cfg["kfi"], cfg["step"] % cfg["kfi"])
+    t0 = time.perf_counter()
+    O.attention_torch_cpu(q, k, v, fp, tk, tv, frames=frames)
+    return time.perf_counter() - t0
+
+
+def cpu_baseline(cfg, flop_tiles, budget_s=15.0):
+    threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    T = cfg["T"]
+    t1 = cpu_sample(cfg, [T // 2], threads)
+    nf = max(1, min(T, int(budget_s / max(t1, 1e-3))))
+    frames = [int(round(i * (T - 1) / max(1, nf - 1))) for i in range(nf)] if nf > 1 else [T // 2]
+    t = cpu_sample(cfg, frames, threads)
+    # per-frame work is identical (constant attended count), so scale by T / frames
+    per_layer = t * T / len(frames)
+    return {"value": round(flop_tiles / per_layer / 1e12, 4), "unit": "TFLOP/s", "cores": threads,
+            "kind": "port", "ms_per_layer": round(per_layer * 1e3, 1),
+            "sample": f"{len(frames)} of {T} query frames x all heads of one {cfg['desc']} layer: "
+                      f"lvsa_sdpa restated (K/V concat + torch fp32 CPU SDPA), scaled by T/frames"}
+
+
+def run_reference(args, cfg):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    flop_tiles, flop_exact = flops_for(cfg)
+    threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    T = cfg["T"]
+    per = []
+    for s in range(args.warmup + args.steps):
+        f = [(s * 7) % T]
+        dt = cpu_sample(cfg, f, threads)
+        if s >= args.warmup:
+            per.append(dt * T)  # seconds per layer
+    per_layer = statistics.mean(per)
+    val = flop_tiles / per_layer / 1e12
+    line = {"impl": "reference", "metric": METRIC, "value": round(val, 4), "unit": "TFLOP/s",
+            "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(per_layer * 1e3 * cfg["layers"], 1),
+            "ms_per_layer": round(per_layer * 1e3, 1), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1)/sqrt(D))",
+            "config": {"workload": args.config, "desc": cfg["desc"], "layers_per_step": cfg["layers"]},
+            "cpu_baseline": {"value": round(val, 4), "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                             "sample": "1 query frame (all heads) per step of one layer, scaled by T"},
+            "e2e": {"value": round(val, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--config", default="cfg2", choices=sorted(CONFIGS))
+    ap.add_argument("--layers", type=int, default=None, help="override layers per step")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    cfg = dict(CONFIGS[args.config])
+    if args.layers:
+        cfg["layers"] = args.layers
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1 or args.gpus > 1:
+        args.cpu_baseline = False
+    if args.impl == "reference":
+        run_reference(args, cfg)
+    else:
+        run_b200(args, cfg)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,140 @@
+/*
+ * lvsa_b200.h -- C ABI of the B200 (sm_100a) LVSA block-sparse attention path.
+ *
+ * Plain C: pointers, sizes and status codes; no torch or CUDA types in the
+ * signatures (a stream is passed as `void*`, i.e. a cudaStream_t / CUstream).
+ * Every buffer is caller-owned device memory; nothing here allocates device
+ * memory and nothing throws across the boundary.  A non-zero return is one of
+ * the LVSA_* status codes below; lvsa_status_str() names it.
+ *
+ * The reference (JiusiServe/LongVideoSparseAttention v1.2.0) has no native
+ * code; each entry point names the Python interface it replaces.
+ */
+#ifndef LVSA_B200_H_
+#define LVSA_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  LVSA_OK = 0,
+  LVSA_ERR_INVALID_ARG = 1,  /* null pointer, negative size, bad enum            */
+  LVSA_ERR_GEOMETRY = 2,     /* pattern/sequence geometry inconsistent           */
+  LVSA_ERR_UNSUPPORTED = 3,  /* head_dim / dtype / block size not built          */
+  LVSA_ERR_ALIGNMENT = 4,    /* pointer or stride violates the 16-byte TMA rule  */
+  LVSA_ERR_CAPACITY = 5,     /* caller buffer smaller than lvsa_mask_layout says */
+  LVSA_ERR_CUDA = 6,         /* a CUDA runtime call failed                       */
+  LVSA_ERR_DEVICE_TIMEOUT = 7 /* a kernel's bounded wait expired (error word)    */
+};
+
+enum { LVSA_DTYPE_BF16 = 0, LVSA_DTYPE_F16 = 1 };
+
+/* Largest total_frames the mask builder accepts. */
+#define LVSA_MAX_FRAMES 2048
+
+/* Sparsity pattern of one denoising step (world = 1 semantics).
+ * Mirrors LVSAMetadata.build(total_latent_frames, num_patches, window_size,
+ * n_first_frames, key_frame_interval, rank=0, world=1, expand_window,
+ * keyframe_offset, boundary_guards)  -- lvsa/sparse_attention.py:339-353.  */
+typedef struct LvsaPattern {
+  int32_t total_frames;       /* T                                          */
+  int32_t num_patches;        /* P, tokens per latent frame                 */
+  int32_t window_size;        /* W (0 = globals only)                       */
+  int32_t n_first_frames;     /* anchor frames 0..n_first-1                 */
+  int32_t key_frame_interval; /* <= 0 means None                            */
+  int32_t keyframe_offset;    /* step % kfi                                 */
+  int32_t expand_window;      /* 0/1                                        */
+  int32_t n_text;             /* text tokens (own segment, dense)           */
+  int32_t block_q;            /* query tile rows (multiple of 16, <= 256)   */
+  int32_t block_k;            /* key tile columns (multiple of 16, <= 256)  */
+  int32_t n_guards;           /* extra global frames (boundary guards)      */
+  const int32_t* guards;      /* HOST array of n_guards frame indices       */
+} LvsaPattern;
+
+/* Sizes of every output of lvsa_build_mask for a pattern. */
+typedef struct LvsaMaskLayout {
+  int32_t n_video;           /* T * P                                        */
+  int32_t n_q_video_tiles;   /* ceil(n_video / block_q)                      */
+  int32_t n_q_tiles;         /* + ceil(n_text / block_q) text query tiles    */
+  int32_t n_k_video_tiles;   /* ceil(n_video / block_k)                      */
+  int32_t n_k_tiles;         /* + ceil(n_text / block_k) text key tiles      */
+  int32_t frame_words;       /* ceil(T / 32): words per attended-frame bitset */
+  int64_t max_nnz;           /* capacity needed for tile_indices/tile_flags  */
+} LvsaMaskLayout;
+
+/* Device output buffers of lvsa_build_mask (all caller-owned). */
+typedef struct LvsaMaskBuffers {
+  int8_t* global_frame_mask;   /* [T]            LVSAMetadata.global_frame_mask */
+  int32_t* window_bounds;      /* [T, 2]         LVSAMetadata.window_bounds     */
+  uint32_t* frame_bits;        /* [T, frame_words] attended frames per frame  */
+  int32_t* attended_indices;   /* [T, T] row-padded; columns [0, C) equal
+                                  LVSAMetadata.attended_indices                 */
+  int32_t* frame_indptr;       /* [T + 1]        LVSAMetadata.fi_indptr         */
+  int32_t* frame_indices;      /* [T * T] first frame_nnz = LVSAMetadata.fi_indices */
+  int32_t* tile_indptr;        /* [n_q_tiles + 1] tile CSR row pointers        */
+  int32_t* tile_indices;       /* [max_nnz]      active key tiles, ascending    */
+  uint8_t* tile_flags;         /* [max_nnz]      bit0: tile needs in-tile mask  */
+  int32_t* counters;           /* [4]: tile nnz, attended C, frame nnz, compact_n */
+} LvsaMaskBuffers;
+
+/* Host-only: sizes for a pattern.  Replaces nothing in the reference (its
+ * builder sizes Python lists as it goes). */
+int lvsa_mask_layout(const LvsaPattern* pattern, LvsaMaskLayout* layout);
+
+/* GPU mask builder: frame-level pattern + tile CSR for one denoising step,
+ * enqueued on `stream` (no host synchronisation).
+ * Replaces LVSAMetadata.build + _build_attended_indices + _build_flashinfer_csr
+ * (lvsa/sparse_attention.py:335-484, :510-547, :550-635), which the reference
+ * re-runs on the host at every keyframe rotation (lvsa/lvsa_processor.py:362-405). */
+int lvsa_build_mask(const LvsaPattern* pattern, const LvsaMaskBuffers* out, void* stream);
+
+/* A [B, N, heads, head_dim] tensor view: element strides, last dim contiguous. */
+typedef struct LvsaTensor {
+  void* ptr;
+  int64_t stride_b;
+  int64_t stride_t;
+  int64_t stride_h;
+} LvsaTensor;
+
+typedef struct LvsaAttnArgs {
+  /* video segment: q/o [B, n_video, heads, D]; k/v [B, n_video, kv_heads, D] */
+  LvsaTensor q, k, v, o;
+  /* text segment (n_text tokens): text_k/text_v required when n_text > 0;
+   * text_q/text_o optional (NULL ptr: text query rows are skipped).          */
+  LvsaTensor text_q, text_k, text_v, text_o;
+  float* lse;       /* optional [B, heads, n_video] natural-log LSE (fp32) */
+  float* text_lse;  /* optional [B, heads, n_text]                          */
+  int32_t batch, n_video, n_text, heads, kv_heads, head_dim, dtype;
+  float scale;      /* <= 0: 1/sqrt(head_dim)                               */
+  /* pattern + tile CSR from lvsa_build_mask (block_q = block_k = 128) */
+  int32_t total_frames, num_patches, frame_words, block_q, block_k;
+  int32_t n_q_video_tiles, n_q_tiles, n_k_video_tiles;
+  const uint32_t* frame_bits;
+  const int32_t* tile_indptr;
+  const int32_t* tile_indices;
+  const uint8_t* tile_flags;
+  int32_t* error_word; /* optional device int: LVSA_ERR_DEVICE_TIMEOUT on a stalled wait */
+} LvsaAttnArgs;
+
+/* Block-sparse attention forward on tcgen05/TMEM, K/V read in place.
+ * Replaces lvsa_sdpa (lvsa/sparse_attention.py:643-706), lvsa_flashinfer
+ * (:709-742), DistributedLVSAProcessor._compute_lvsa_flashinfer with its text
+ * LSE merge (lvsa/lvsa_processor.py:832-913) and the dense encoder-query
+ * attention _compute_full_attention (:710-735): video rows attend their
+ * frame's attended set plus all text, text rows attend everything. */
+int lvsa_attn_fwd(const LvsaAttnArgs* args, void* stream);
+
+/* Human-readable name of a status code. */
+const char* lvsa_status_str(int status);
+
+/* ABI version (major * 100 + minor). */
+int lvsa_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* LVSA_B200_H_ */

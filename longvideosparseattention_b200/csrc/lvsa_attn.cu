@@ -1,0 +1,511 @@
+// Block-sparse LVSA attention forward for sm_100a (tcgen05 + TMEM + TMA).
+//
+// One CTA per (128-row query tile, head, batch).  Warp roles:
+//   warps 0-3  softmax: thread r owns query row r (= TMEM lane r); reads S
+//              from TMEM, applies the in-tile frame mask on flagged tiles,
+//              online softmax in the log2 domain with lazy O rescaling,
+//              writes P (bf16/f16) to TMEM, final O / l epilogue.
+//   warp 4     TMA producer: Q once, then K and V tiles of the row's CSR
+//              list, read in place from the [B, N, H, D] tensors.
+//   warp 5     TMEM allocator + single-thread tcgen05.mma issuer:
+//              S_j = Q K_j^T (SS), then O += P_{j-1} V_{j-1} (TS, P from TMEM).
+// TMEM columns: S0 [0,128) S1 [128,256) O [256,256+D) P0 [384,448) P1 [448,512).
+//
+// Semantics follow lvsa_sdpa (lvsa/sparse_attention.py:643-706) with the
+// processor's text handling (lvsa/lvsa_processor.py:545-549, 584-591):
+// every video query attends to all tokens of its frame's attended set and all
+// text tokens; text queries attend to everything.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+#include <type_traits>
+
+#include "../../include/lvsa_b200.h"
+#include "lvsa_ptx.cuh"
+
+namespace lvsa {
+namespace {
+
+constexpr int kBM = 128;          // query rows per tile
+constexpr int kBN = 128;          // key tokens per tile
+constexpr int kChunk = 128 * 128; // one 128-row x 128-byte swizzle-128B slab
+constexpr int kThreads = 192;
+constexpr uint32_t kTmemCols = 512;
+constexpr float kNegInf = -INFINITY;
+
+struct AttnParams {
+  void* o;
+  void* text_o;
+  float* lse;
+  float* text_lse;
+  int64_t o_sb, o_st, o_sh, to_sb, to_st, to_sh;
+  int n_video, n_text, heads, kv_heads, T, P, words, nqv, nkv;
+  float scale_log2;
+  const uint32_t* frame_bits;
+  const int32_t* indptr;
+  const int32_t* indices;
+  const uint8_t* flags;
+  int* err;
+};
+
+template <int D, int STAGES>
+struct Smem {
+  static constexpr int kCh = D / 64;               // 128-byte column slabs per row
+  static constexpr int kTile = kCh * kChunk;       // bytes of one 128 x D tile
+  static constexpr int kQ = 0;
+  static constexpr int kK = kTile;
+  static constexpr int kV = kK + STAGES * kTile;
+  static constexpr int kBar = kV + STAGES * kTile;
+  static constexpr int kNumBars = 1 + 3 * STAGES + 6 + 1;
+  static constexpr int kMisc = kBar + kNumBars * 8;
+  static constexpr int kBytes = kMisc + 16 + 1024;  // + alignment slack
+};
+
+__device__ __forceinline__ uint32_t pack2(float a, float b, bool bf16) {
+  if (bf16) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+  __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+__device__ __forceinline__ void set_cols(uint32_t (&am)[4], int a, int b) {  // [a, b)
+#pragma unroll
+  for (int w = 0; w < 4; ++w) {
+    const int lo = max(a, w * 32), hi = min(b, w * 32 + 32);
+    if (lo < hi) {
+      const int n = hi - lo;
+      const uint32_t m = (n == 32) ? 0xFFFFFFFFu : ((1u << n) - 1u);
+      am[w] |= m << (lo - w * 32);
+    }
+  }
+}
+
+template <int D, int STAGES, bool kBf16>
+__global__ void __launch_bounds__(kThreads, 1)
+    lvsa_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_tq,
+                     const __grid_constant__ CUtensorMap tm_tk, const __grid_constant__ CUtensorMap tm_tv,
+                     const AttnParams prm) {
+  using L = Smem<D, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem + L::kQ;
+  uint8_t* sK = smem + L::kK;
+  uint8_t* sV = smem + L::kV;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBar);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;
+  uint64_t* v_full = k_full + STAGES;
+  uint64_t* kv_empty = v_full + STAGES;
+  uint64_t* s_full = kv_empty + STAGES;  // [2]
+  uint64_t* p_full = s_full + 2;         // [2]
+  uint64_t* pv_done = p_full + 2;        // [2]
+  uint64_t* drain = pv_done + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMisc);
+  volatile int* abort = reinterpret_cast<volatile int*>(smem + L::kMisc + 4);
+  volatile int* never = reinterpret_cast<volatile int*>(smem + L::kMisc + 8);  // stays 0: drain waits
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int beg = prm.indptr[row];
+  const int n = prm.indptr[row + 1] - beg;
+  const bool text_row = row >= prm.nqv;
+  const int tok0 = (text_row ? row - prm.nqv : row) * kBM;
+  const int hk = h / (prm.heads / prm.kv_heads);
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&pv_done[i], 1);
+    }
+    mbar_init(drain, 1);
+    *abort = 0;
+    *never = 0;
+    fence_mbar_init();
+  }
+  if (warp == 5) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS = tmem, tO = tmem + 256, tP = tmem + 384;
+
+  if (warp == 4) {
+    // ---------------------------------------------------------- producer
+    if (lane == 0 && n > 0) {
+      const CUtensorMap* mq = text_row ? &tm_tq : &tm_q;
+      tma_prefetch_desc(mq);
+      tma_prefetch_desc(&tm_k);
+      tma_prefetch_desc(&tm_v);
+      mbar_expect_tx(q_full, L::kTile);
+#pragma unroll
+      for (int c = 0; c < L::kCh; ++c) tma_load_4d(sQ + c * kChunk, mq, q_full, c * 64, h, tok0, b);
+      int issued = 0;
+      for (int j = 0; j < n; ++j) {
+        const int s = j % STAGES;
+        if (j >= STAGES && !mbar_wait(&kv_empty[s], ((j / STAGES) - 1) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT))
+          break;
+        const int kt = prm.indices[beg + j];
+        const bool tt = kt >= prm.nkv;
+        const int ktok = (tt ? kt - prm.nkv : kt) * kBN;
+        const CUtensorMap* mk = tt ? &tm_tk : &tm_k;
+        const CUtensorMap* mv = tt ? &tm_tv : &tm_v;
+        mbar_expect_tx(&k_full[s], L::kTile);
+#pragma unroll
+        for (int c = 0; c < L::kCh; ++c)
+          tma_load_4d(sK + s * L::kTile + c * kChunk, mk, &k_full[s], c * 64, hk, ktok, b);
+        mbar_expect_tx(&v_full[s], L::kTile);
+#pragma unroll
+        for (int c = 0; c < L::kCh; ++c)
+          tma_load_4d(sV + s * L::kTile + c * kChunk, mv, &v_full[s], c * 64, hk, ktok, b);
+        issued = j + 1;
+      }
+      if (*abort) {
+        // Drain our own copies still in flight before the CTA retires.
+        mbar_wait(q_full, 0, never, nullptr, 0);
+        for (int j = max(0, issued - STAGES); j < issued; ++j) {
+          const int s = j % STAGES;
+          mbar_wait(&k_full[s], (j / STAGES) & 1, never, nullptr, 0);
+          mbar_wait(&v_full[s], (j / STAGES) & 1, never, nullptr, 0);
+        }
+      }
+    }
+  } else if (warp == 5) {
+    // ---------------------------------------------------------- MMA issuer
+    if (lane == 0 && n > 0) {
+      constexpr uint32_t idS = idesc_f16(kBM, kBN, kBf16, false);
+      constexpr uint32_t idO = idesc_f16(kBM, D, kBf16, true);
+      const uint32_t q_base = smem_u32(sQ), k_base = smem_u32(sK), v_base = smem_u32(sV);
+      if (mbar_wait(q_full, 0, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT)) {
+        for (int j = 0; j <= n; ++j) {
+          if (j < n) {
+            const int s = j % STAGES;
+            if (!mbar_wait(&k_full[s], (j / STAGES) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT)) break;
+            tc_fence_after();
+            const uint32_t dS = tS + (j & 1) * 128;
+            const uint32_t kb = k_base + s * L::kTile;
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk) {
+              const uint32_t off = (kk >> 2) * kChunk + (kk & 3) * 32;
+              mma_ss(dS, sdesc_sw128(q_base + off, 16, 1024), sdesc_sw128(kb + off, 16, 1024), idS, kk > 0);
+            }
+            mma_commit(&s_full[j & 1]);
+          }
+          if (j > 0) {
+            const int jj = j - 1, bb = jj & 1, s = jj % STAGES;
+            if (!mbar_wait(&p_full[bb], (jj >> 1) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT)) break;
+            if (!mbar_wait(&v_full[s], (jj / STAGES) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT)) break;
+            tc_fence_after();
+            const uint32_t vb = v_base + s * L::kTile;
+#pragma unroll
+            for (int kk = 0; kk < kBN / 16; ++kk)
+              mma_ts(tO, tP + bb * 64 + kk * 8, sdesc_sw128(vb + kk * 2048, kChunk, 1024), idO, (jj > 0 || kk > 0));
+            mma_commit(&pv_done[bb]);
+            mma_commit(&kv_empty[s]);
+          }
+        }
+      }
+      // Make sure every MMA this thread issued has retired before TMEM is freed.
+      mma_commit(drain);
+      mbar_wait(drain, 0, never, nullptr, 0);
+    }
+  } else {
+    // ---------------------------------------------------------- softmax
+    const int r = threadIdx.x;
+    const int seg_len = text_row ? prm.n_text : prm.n_video;
+    const int tok = tok0 + r;
+    const bool valid = tok < seg_len;
+    const int fq = text_row ? 0 : min(tok / prm.P, prm.T - 1);
+    const uint32_t* fbits = prm.frame_bits + static_cast<size_t>(fq) * prm.words;
+    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    const float sl2 = prm.scale_log2;
+    float m = kNegInf, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n; ++j) {
+      const int bb = j & 1;
+      ok = __all_sync(0xFFFFFFFFu, mbar_wait(&s_full[bb], (j >> 1) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT));
+      if (!ok) break;
+      tc_fence_after();
+      float s[kBN];
+#pragma unroll
+      for (int c = 0; c < kBN / 32; ++c) {
+        uint32_t t[32];
+        tmem_ld32(tS + lane_base + bb * 128 + c * 32, t);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(t[i]);
+      }
+      if (prm.flags[beg + j]) {
+        uint32_t am[4] = {0u, 0u, 0u, 0u};
+        const int kt = prm.indices[beg + j];
+        if (kt >= prm.nkv) {
+          set_cols(am, 0, min(kBN, prm.n_text - (kt - prm.nkv) * kBN));
+        } else if (text_row) {
+          set_cols(am, 0, min(kBN, prm.n_video - kt * kBN));
+        } else {
+          const int ks = kt * kBN, kend = min(ks + kBN, prm.n_video);
+          int f = ks / prm.P, c0 = 0;
+          while (ks + c0 < kend) {
+            const int ce = min((f + 1) * prm.P, kend) - ks;
+            if ((fbits[f >> 5] >> (f & 31)) & 1u) set_cols(am, c0, ce);
+            c0 = ce;
+            ++f;
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < kBN; ++i)
+          if (!((am[i >> 5] >> (i & 31)) & 1u)) s[i] = kNegInf;
+      }
+      float mx = s[0];
+#pragma unroll
+      for (int i = 1; i < kBN; ++i) mx = fmaxf(mx, s[i]);
+      const float m_new = fmaxf(m, mx * sl2);
+      if (j == 0) {
+        m = m_new;
+      } else {
+        const bool need = m_new > m + 8.0f;
+        if (__any_sync(0xFFFFFFFFu, need)) {
+          const float alpha = need ? ex2_approx(m - m_new) : 1.f;
+          if (need) m = m_new;
+          ok = __all_sync(0xFFFFFFFFu, mbar_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, abort, prm.err,
+                                                 LVSA_ERR_DEVICE_TIMEOUT));
+          if (!ok) break;
+          tc_fence_after();
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t t[32];
+            tmem_ld32(tO + lane_base + c * 32, t);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) t[i] = __float_as_uint(__uint_as_float(t[i]) * alpha);
+            tmem_st32(tO + lane_base + c * 32, t);
+          }
+          l *= alpha;
+        }
+      }
+      const float mu = (m == kNegInf) ? 0.f : m;
+      float sum = 0.f;
+#pragma unroll
+      for (int i = 0; i < kBN; ++i) {
+        s[i] = ex2_approx(fmaf(s[i], sl2, -mu));
+        sum += s[i];
+      }
+      l += sum;
+      if (j >= 2) {
+        ok = __all_sync(0xFFFFFFFFu, mbar_wait(&pv_done[bb], ((j - 2) >> 1) & 1, abort, prm.err,
+                                               LVSA_ERR_DEVICE_TIMEOUT));
+        if (!ok) break;
+        tc_fence_after();
+      }
+#pragma unroll
+      for (int hcol = 0; hcol < 2; ++hcol) {
+        uint32_t pk[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) pk[i] = pack2(s[hcol * 64 + 2 * i], s[hcol * 64 + 2 * i + 1], kBf16);
+        tmem_st32(tP + lane_base + bb * 64 + hcol * 32, pk);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&p_full[bb]);
+    }
+    // ---------------------------------------------------------- epilogue
+    using Elem = typename std::conditional<kBf16, __nv_bfloat16, __half>::type;
+    Elem* obase = nullptr;
+    float* lse = nullptr;
+    if (text_row) {
+      if (prm.text_o)
+        obase = reinterpret_cast<Elem*>(prm.text_o) + b * prm.to_sb + static_cast<int64_t>(tok) * prm.to_st +
+                h * prm.to_sh;
+      if (prm.text_lse) lse = prm.text_lse + (static_cast<int64_t>(b) * prm.heads + h) * prm.n_text + tok;
+    } else {
+      obase = reinterpret_cast<Elem*>(prm.o) + b * prm.o_sb + static_cast<int64_t>(tok) * prm.o_st + h * prm.o_sh;
+      if (prm.lse) lse = prm.lse + (static_cast<int64_t>(b) * prm.heads + h) * prm.n_video + tok;
+    }
+    if (ok && n > 0) {
+      ok = __all_sync(0xFFFFFFFFu, mbar_wait(&pv_done[(n - 1) & 1], ((n - 1) >> 1) & 1, abort, prm.err,
+                                             LVSA_ERR_DEVICE_TIMEOUT));
+      if (ok) {
+        tc_fence_after();
+        const float inv = (l > 0.f) ? 1.f / l : 0.f;
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t t[32];
+          tmem_ld32(tO + lane_base + c * 32, t);
+          if (valid && obase) {
+            uint32_t pk[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              pk[i] = pack2(__uint_as_float(t[2 * i]) * inv, __uint_as_float(t[2 * i + 1]) * inv, kBf16);
+            uint4* dst = reinterpret_cast<uint4*>(obase + c * 32);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+          }
+        }
+        if (valid && lse) *lse = (l > 0.f) ? (m + __log2f(l)) * 0.69314718055994531f : kNegInf;
+      }
+    } else if (n == 0 && valid) {
+      if (obase) {
+        uint4* dst = reinterpret_cast<uint4*>(obase);
+#pragma unroll
+        for (int i = 0; i < D / 8; ++i) dst[i] = make_uint4(0u, 0u, 0u, 0u);
+      }
+      if (lse) *lse = kNegInf;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// ------------------------------------------------------------------ host side
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// [B, N, Hx, D] view -> 4-D map (D, Hx, N, B) with a (64, 1, 128, 1) box, 128B swizzle.
+int make_map(CUtensorMap* map, const LvsaTensor& t, int B, int N, int Hx, int D, bool bf16) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return LVSA_ERR_CUDA;
+  if (!t.ptr || N < 1) return LVSA_ERR_INVALID_ARG;
+  const int64_t es = 2;
+  if ((reinterpret_cast<uintptr_t>(t.ptr) & 15) || (t.stride_h * es) % 16 || (t.stride_t * es) % 16 ||
+      (B > 1 && (t.stride_b * es) % 16))
+    return LVSA_ERR_ALIGNMENT;
+  if (t.stride_h < D || t.stride_t < 1) return LVSA_ERR_INVALID_ARG;
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(Hx), static_cast<cuuint64_t>(N),
+                        static_cast<cuuint64_t>(B)};
+  const int64_t sb = (B > 1) ? t.stride_b : t.stride_t * N;
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(t.stride_h * es), static_cast<cuuint64_t>(t.stride_t * es),
+                           static_cast<cuuint64_t>(sb * es)};
+  cuuint32_t box[4] = {64, 1, static_cast<cuuint32_t>(kBM), 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, t.ptr, dims,
+                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? LVSA_OK : LVSA_ERR_ALIGNMENT;
+}
+
+template <int D, int STAGES, bool kBf16>
+int launch(const LvsaAttnArgs* a, cudaStream_t stream) {
+  using L = Smem<D, STAGES>;
+  CUtensorMap mq, mk, mv, mtq, mtk, mtv;
+  int st;
+  if ((st = make_map(&mq, a->q, a->batch, a->n_video, a->heads, D, kBf16))) return st;
+  if ((st = make_map(&mk, a->k, a->batch, a->n_video, a->kv_heads, D, kBf16))) return st;
+  if ((st = make_map(&mv, a->v, a->batch, a->n_video, a->kv_heads, D, kBf16))) return st;
+  const bool text_rows = a->n_text > 0 && a->text_q.ptr != nullptr;
+  if (a->n_text > 0) {
+    if ((st = make_map(&mtk, a->text_k, a->batch, a->n_text, a->kv_heads, D, kBf16))) return st;
+    if ((st = make_map(&mtv, a->text_v, a->batch, a->n_text, a->kv_heads, D, kBf16))) return st;
+  } else {
+    mtk = mk;
+    mtv = mv;
+  }
+  if (text_rows) {
+    if ((st = make_map(&mtq, a->text_q, a->batch, a->n_text, a->heads, D, kBf16))) return st;
+  } else {
+    mtq = mq;
+  }
+  AttnParams p;
+  p.o = a->o.ptr;
+  p.text_o = text_rows ? a->text_o.ptr : nullptr;
+  p.lse = a->lse;
+  p.text_lse = text_rows ? a->text_lse : nullptr;
+  p.o_sb = a->o.stride_b; p.o_st = a->o.stride_t; p.o_sh = a->o.stride_h;
+  p.to_sb = a->text_o.stride_b; p.to_st = a->text_o.stride_t; p.to_sh = a->text_o.stride_h;
+  p.n_video = a->n_video; p.n_text = a->n_text; p.heads = a->heads; p.kv_heads = a->kv_heads;
+  p.T = a->total_frames; p.P = a->num_patches; p.words = a->frame_words;
+  p.nqv = a->n_q_video_tiles; p.nkv = a->n_k_video_tiles;
+  const float scale = a->scale > 0.f ? a->scale : 1.0f / std::sqrt(static_cast<float>(D));
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.frame_bits = a->frame_bits; p.indptr = a->tile_indptr; p.indices = a->tile_indices; p.flags = a->tile_flags;
+  p.err = a->error_word;
+
+  auto kern = lvsa_attn_kernel<D, STAGES, kBf16>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes) != cudaSuccess)
+    return LVSA_ERR_CUDA;
+  const int rows = text_rows ? a->n_q_tiles : a->n_q_video_tiles;
+  dim3 grid(rows, a->heads, a->batch);
+  kern<<<grid, kThreads, L::kBytes, stream>>>(mq, mk, mv, mtq, mtk, mtv, p);
+  return cudaGetLastError() == cudaSuccess ? LVSA_OK : LVSA_ERR_CUDA;
+}
+
+}  // namespace
+}  // namespace lvsa
+
+extern "C" int lvsa_attn_fwd(const LvsaAttnArgs* a, void* stream) {
+  using namespace lvsa;
+  if (!a || !a->q.ptr || !a->k.ptr || !a->v.ptr || !a->o.ptr || !a->frame_bits || !a->tile_indptr ||
+      !a->tile_indices || !a->tile_flags)
+    return LVSA_ERR_INVALID_ARG;
+  if (a->batch < 1 || a->n_video < 1 || a->n_text < 0 || a->heads < 1 || a->kv_heads < 1 ||
+      a->heads % a->kv_heads)
+    return LVSA_ERR_INVALID_ARG;
+  if (a->block_q != kBM || a->block_k != kBN) return LVSA_ERR_UNSUPPORTED;
+  if (a->total_frames < 1 || a->num_patches < 1 ||
+      static_cast<long long>(a->total_frames) * a->num_patches != a->n_video)
+    return LVSA_ERR_GEOMETRY;
+  if (a->n_q_video_tiles != (a->n_video + kBM - 1) / kBM || a->n_k_video_tiles != (a->n_video + kBN - 1) / kBN ||
+      a->frame_words != (a->total_frames + 31) / 32)
+    return LVSA_ERR_GEOMETRY;
+  if (a->n_text > 0 && (!a->text_k.ptr || !a->text_v.ptr)) return LVSA_ERR_INVALID_ARG;
+  if (a->n_text > 0 && a->text_q.ptr && !a->text_o.ptr) return LVSA_ERR_INVALID_ARG;
+  if (a->n_text > 0 && a->n_q_tiles != a->n_q_video_tiles + (a->n_text + kBM - 1) / kBM) return LVSA_ERR_GEOMETRY;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool bf16 = a->dtype == LVSA_DTYPE_BF16;
+  if (a->dtype != LVSA_DTYPE_BF16 && a->dtype != LVSA_DTYPE_F16) return LVSA_ERR_UNSUPPORTED;
+  switch (a->head_dim) {
+    case 128: return bf16 ? launch<128, 2, true>(a, s) : launch<128, 2, false>(a, s);
+    case 64: return bf16 ? launch<64, 4, true>(a, s) : launch<64, 4, false>(a, s);
+    default: return LVSA_ERR_UNSUPPORTED;
+  }
+}
+
+extern "C" const char* lvsa_status_str(int status) {
+  switch (status) {
+    case LVSA_OK: return "ok";
+    case LVSA_ERR_INVALID_ARG: return "invalid argument";
+    case LVSA_ERR_GEOMETRY: return "geometry mismatch";
+    case LVSA_ERR_UNSUPPORTED: return "unsupported head_dim/dtype/block size";
+    case LVSA_ERR_ALIGNMENT: return "pointer or stride not 16-byte aligned for TMA";
+    case LVSA_ERR_CAPACITY: return "buffer capacity too small";
+    case LVSA_ERR_CUDA: return "CUDA runtime error";
+    case LVSA_ERR_DEVICE_TIMEOUT: return "device wait timed out";
+    default: return "unknown status";
+  }
+}
+
+extern "C" int lvsa_abi_version(void) { return 100; }

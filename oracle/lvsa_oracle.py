@@ -339,3 +339,33 @@ def attention(q, k, v, pattern: Dict, text_q=None, text_k=None, text_v=None,
                 vv = np.concatenate([v[b, :, kh], tv[b, :, kh]])
                 out_text[b, :, h] = _softmax_av(tq[b, :, h], kk, vv, scale)
     return out, out_text
+
+
+def attention_torch_cpu(q, k, v, pattern: Dict, text_k=None, text_v=None,
+                        frames: Optional[Sequence[int]] = None):
+    """The reference's own CPU arithmetic for the video rows: per query frame,
+    concatenate the anchor and window K/V (plus text) and call torch's fp32
+    scaled_dot_product_attention -- lvsa/sparse_attention.py:674-704 with the
+    text K/V appended as lvsa/lvsa_processor.py:545-549.  Multithreaded by
+    torch; used as the timed CPU baseline.  Inputs: torch CPU [B, S, H, D]."""
+    import torch
+    import torch.nn.functional as F
+    P = pattern["P"]
+    B, N, H, D = q.shape
+    gqa = k.shape[2] != H
+    gidx = pattern["global_indices"]
+    ar = torch.arange(P)
+    gtok = (torch.tensor(gidx)[:, None] * P + ar[None, :]).reshape(-1)
+    kg, vg = k[:, gtok], v[:, gtok]
+    if text_k is not None and text_k.shape[1] > 0:
+        kg, vg = torch.cat([kg, text_k], 1), torch.cat([vg, text_v], 1)
+    out = torch.empty_like(q)
+    for f in (range(pattern["T"]) if frames is None else frames):
+        lo, hi = (int(x) for x in pattern["window_bounds"][f])
+        win = [w for w in range(lo, hi + 1) if w not in pattern["global_set"]]
+        kc = torch.cat([kg] + [k[:, w * P:(w + 1) * P] for w in win], 1)
+        vc = torch.cat([vg] + [v[:, w * P:(w + 1) * P] for w in win], 1)
+        o = F.scaled_dot_product_attention(q[:, f * P:(f + 1) * P].transpose(1, 2), kc.transpose(1, 2),
+                                           vc.transpose(1, 2), enable_gqa=gqa)
+        out[:, f * P:(f + 1) * P] = o.transpose(1, 2)
+    return out

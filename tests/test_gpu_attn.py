@@ -1,0 +1,148 @@
+"""Block-sparse attention on the GPU (through the C ABI) vs the reference.
+
+Tolerance (stated by the task): bf16 output vs the fp32 reference on the same
+bf16-representable inputs, max-abs <= 2e-2 and mean-abs <= 2e-3.
+"""
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import lvsa_oracle as O
+from tests.conftest import GOLDEN
+from tests.gpu_util import assert_close, seeded, to_np
+
+pytestmark = pytest.mark.gpu
+
+ATTN = sorted(f[5:-4] for f in os.listdir(GOLDEN) if f.startswith("attn_"))
+
+
+def _run(q, k, v, T, P, W, nf, kfi, off, tq=None, tk=None, tv=None, lse=False, scale=None):
+    from longvideosparseattention_b200 import block_sparse_attention, build_block_mask
+    nt = 0 if tk is None else tk.shape[1]
+    m = build_block_mask(T, P, W, nf, kfi, off, True, nt, device=q.device)
+    res = block_sparse_attention(q, k, v, m, tq, tk, tv, scale=scale, return_lse=lse)
+    torch.cuda.synchronize()
+    from longvideosparseattention_b200 import check_device_errors
+    check_device_errors(q.device)
+    return res
+
+
+@pytest.mark.parametrize("name", ATTN)
+def test_attention_matches_reference_golden(name):
+    z = np.load(os.path.join(GOLDEN, f"attn_{name}.npz"))
+    T, P, H, Hkv, D, W, nf, kfi, off, nt, B, seed = z["params"].tolist()
+    dev = "cuda"
+    cv = lambda a: torch.from_numpy(a).to(torch.bfloat16).to(dev)  # exact: values are bf16
+    q, k, v = cv(z["q"]), cv(z["k"]), cv(z["v"])
+    tq = tk = tv = None
+    if nt > 0:
+        tq, tk, tv = cv(z["text_q"]), cv(z["text_k"]), cv(z["text_v"])
+    out, tout = _run(q, k, v, T, P, W, nf, kfi, off, tq, tk, tv)
+    assert out.dtype == torch.bfloat16 and out.shape == q.shape
+    assert_close(to_np(out), z["out"], what=f"{name} video rows")
+    if nt > 0:
+        assert_close(to_np(tout), z["text_out"], what=f"{name} text rows")
+
+
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_attention_random_vs_oracle(D, dtype):
+    T, P, H, W, kfi, off, nt = 11, 97, 3, 2, 3, 1, 70
+    B = 2
+    q = seeded((B, T * P, H, D), 1, dtype)
+    k = seeded((B, T * P, H, D), 2, dtype)
+    v = seeded((B, T * P, H, D), 3, dtype)
+    tq = seeded((B, nt, H, D), 4, dtype)
+    tk = seeded((B, nt, H, D), 5, dtype)
+    tv = seeded((B, nt, H, D), 6, dtype)
+    out, tout = _run(q, k, v, T, P, W, 1, kfi, off, tq, tk, tv)
+    fp = O.frame_pattern(T, P, W, 1, kfi, off)
+    want, twant = O.attention(to_np(q), to_np(k), to_np(v), fp, to_np(tq), to_np(tk), to_np(tv))
+    assert_close(to_np(out), want, what="video")
+    assert_close(to_np(tout), twant, what="text")
+
+
+def test_attention_gqa_strided_views_and_lse():
+    # q/k/v as strided views of one packed [B, N, 3, H, D] projection output
+    T, P, H, Hkv, D = 6, 200, 4, 2, 128
+    N = T * P
+    qkv = seeded((1, N, 3 * H * D), 7).view(1, N, 3, H, D)
+    q = qkv[:, :, 0]
+    k = qkv[:, :, 1, :Hkv]
+    v = qkv[:, :, 2, :Hkv]
+    out, _, lse, _ = _run(q, k, v, T, P, 1, 1, 2, 1, lse=True)
+    fp = O.frame_pattern(T, P, 1, 1, 2, 1)
+    want, _ = O.attention(to_np(q), to_np(k), to_np(v), fp)
+    assert_close(to_np(out), want, what="gqa")
+    # LSE (natural log) against a direct float64 computation for a few rows
+    qn, kn = to_np(q).astype(np.float64), to_np(k).astype(np.float64)
+    for f, t in [(0, 5), (3, 650), (5, 1199)]:
+        idx = np.concatenate([np.arange(g * P, (g + 1) * P) for g in fp["attended"][t // P]])
+        for h in range(H):
+            s = kn[0, idx, h // 2] @ qn[0, t, h] / np.sqrt(D)
+            ref = np.log(np.exp(s - s.max()).sum()) + s.max()
+            assert abs(lse[0, h, t].item() - ref) < 2e-3
+
+
+def test_attention_fp32_inputs_round_to_bf16():
+    T, P, H, D = 4, 64, 2, 64
+    q = seeded((1, T * P, H, D), 11, torch.float32)
+    k = seeded((1, T * P, H, D), 12, torch.float32)
+    v = seeded((1, T * P, H, D), 13, torch.float32)
+    out, _ = _run(q, k, v, T, P, 1, 1, 2, 0)
+    assert out.dtype == torch.float32
+    fp = O.frame_pattern(T, P, 1, 1, 2, 0)
+    want, _ = O.attention(to_np(q), to_np(k), to_np(v), fp)
+    assert_close(to_np(out), want, max_abs=3e-2, what="fp32 in")
+
+
+def test_attention_dense_when_every_frame_is_global():
+    # kfi = 1 makes every frame an anchor: LVSA == dense attention (torch SDPA on the GPU).
+    T, P, H, D = 12, 300, 4, 128
+    q = seeded((1, T * P, H, D), 21)
+    k = seeded((1, T * P, H, D), 22)
+    v = seeded((1, T * P, H, D), 23)
+    out, _ = _run(q, k, v, T, P, 2, 1, 1, 0)
+    ref = torch.nn.functional.scaled_dot_product_attention(
+        q.float().transpose(1, 2), k.float().transpose(1, 2), v.float().transpose(1, 2)).transpose(1, 2)
+    assert_close(to_np(out), to_np(ref), what="dense")
+
+
+@pytest.mark.parametrize("cfg", [
+    dict(name="cfg2", T=81, P=1560, H=12, D=128, W=2, kfi=4, off=0, nt=0, frames=[0, 40, 80]),
+    dict(name="cfg3", T=121, P=1560, H=12, D=128, W=2, kfi=4, off=3, nt=0, frames=[1, 77]),
+    dict(name="cfg4", T=49, P=1590, H=16, D=128, W=2, kfi=4, off=0, nt=256, frames=[0, 24, 48]),
+    dict(name="cfg5", T=49, P=1350, H=48, D=64, W=1, kfi=3, off=0, nt=226, frames=[0, 25]),
+])
+def test_attention_baseline_configs_sampled(cfg):
+    """Full-size BASELINE geometries; oracle on sampled frames / heads, plus
+    the size-independent property that V == 1 gives exactly 1 everywhere."""
+    T, P, H, D, nt = cfg["T"], cfg["P"], cfg["H"], cfg["D"], cfg["nt"]
+    N = T * P
+    sc = 1.0 / np.sqrt(D)
+    q = seeded((1, N, H, D), 31, scale=sc)
+    k = seeded((1, N, H, D), 32, scale=sc)
+    v = seeded((1, N, H, D), 33)
+    tq = tk = tv = None
+    if nt:
+        tq, tk, tv = seeded((1, nt, H, D), 34, scale=sc), seeded((1, nt, H, D), 35, scale=sc), \
+            seeded((1, nt, H, D), 36)
+    out, tout = _run(q, k, v, T, P, cfg["W"], 1, cfg["kfi"], cfg["off"], tq, tk, tv)
+    fp = O.frame_pattern(T, P, cfg["W"], 1, cfg["kfi"], cfg["off"])
+    heads = [0, H // 2, H - 1]
+    want, twant = O.attention(to_np(q), to_np(k), to_np(v), fp,
+                              None if tq is None else to_np(tq), None if tk is None else to_np(tk),
+                              None if tv is None else to_np(tv), frames=cfg["frames"], heads=heads)
+    assert_close(to_np(out), want, what=cfg["name"])
+    if nt:
+        assert_close(to_np(tout), twant, what=cfg["name"] + " text")
+    ones = torch.ones_like(v)
+    o1, t1 = _run(q, k, ones, T, P, cfg["W"], 1, cfg["kfi"], cfg["off"], tq, tk,
+                  None if tv is None else torch.ones_like(tv))
+    # P is rounded to bf16 for the PV MMA while l sums fp32 P: 1 within bf16 rounding.
+    assert (o1.float() - 1).abs().max().item() <= 1e-2, "V == 1 must give 1 (coverage / normalisation)"
+    if nt:
+        assert (t1.float() - 1).abs().max().item() <= 1e-2
