@@ -121,9 +121,11 @@ def build_block_mask(total_frames: int, num_patches: int, window_size: int, n_fi
     pat, lay, _keep = mask_layout(total_frames, num_patches, window_size, n_first_frames,
                                   key_frame_interval, keyframe_offset, expand_window, n_text,
                                   block_q, block_k, boundary_guards)
-    device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    device = torch.device(device) if device is not None else torch.device("cuda")
     if device.type != "cuda":
         raise RuntimeError("build_block_mask needs a CUDA device (no CPU fallback)")
+    if device.index is None:
+        device = torch.device("cuda", torch.cuda.current_device())
     T = int(total_frames)
     same = (reuse is not None and reuse.device == device and reuse.total_frames == T
             and reuse.num_patches == num_patches and reuse.n_text == n_text
