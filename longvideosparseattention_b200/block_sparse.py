@@ -19,6 +19,12 @@ from . import _native as N
 
 _ERR_WORDS: Dict[int, torch.Tensor] = {}
 
+# Tile shape the attention kernel consumes: 256 query rows (two tcgen05 M=128
+# tiles sharing every K/V tile) x 128 keys.  The mask builder accepts others
+# (multiples of 16 up to 256) for analysis.
+ATTN_BLOCK_Q = 256
+ATTN_BLOCK_K = 128
+
 
 def _stream_ptr(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
@@ -94,8 +100,8 @@ class BlockMask:
 
 def mask_layout(total_frames: int, num_patches: int, window_size: int, n_first_frames: int,
                 key_frame_interval: Optional[int], keyframe_offset: int = 0,
-                expand_window: bool = True, n_text: int = 0, block_q: int = 128,
-                block_k: int = 128, boundary_guards: Optional[Sequence[int]] = None):
+                expand_window: bool = True, n_text: int = 0, block_q: int = ATTN_BLOCK_Q,
+                block_k: int = ATTN_BLOCK_K, boundary_guards: Optional[Sequence[int]] = None):
     lib = N.load()
     guards = list(boundary_guards or [])
     garr = (ctypes.c_int32 * max(1, len(guards)))(*guards)
@@ -110,8 +116,8 @@ def mask_layout(total_frames: int, num_patches: int, window_size: int, n_first_f
 
 def build_block_mask(total_frames: int, num_patches: int, window_size: int, n_first_frames: int,
                      key_frame_interval: Optional[int], keyframe_offset: int = 0,
-                     expand_window: bool = True, n_text: int = 0, block_q: int = 128,
-                     block_k: int = 128, boundary_guards: Optional[Sequence[int]] = None,
+                     expand_window: bool = True, n_text: int = 0, block_q: int = ATTN_BLOCK_Q,
+                     block_k: int = ATTN_BLOCK_K, boundary_guards: Optional[Sequence[int]] = None,
                      device: Optional[torch.device] = None,
                      reuse: Optional[BlockMask] = None) -> BlockMask:
     """Build the step's pattern on the GPU (4 small kernels, no host sync).
@@ -210,6 +216,9 @@ def block_sparse_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, ma
     B, Nv, H, D = q.shape
     Hkv = k.shape[2]
     Nt = 0 if text_k is None else int(text_k.shape[1])
+    if (mask.block_q, mask.block_k) != (ATTN_BLOCK_Q, ATTN_BLOCK_K):
+        raise ValueError(f"the attention kernel needs a {ATTN_BLOCK_Q}x{ATTN_BLOCK_K} tile CSR, "
+                         f"got {mask.block_q}x{mask.block_k}")
     if Nv != mask.n_video or Nt != mask.n_text:
         raise AssertionError(f"sequence ({Nv} video, {Nt} text) does not match the mask "
                              f"({mask.n_video} video, {mask.n_text} text)")

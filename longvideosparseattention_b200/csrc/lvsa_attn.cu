@@ -32,12 +32,18 @@
 namespace lvsa {
 namespace {
 
-constexpr int kBM = 128;          // query rows per tile
-constexpr int kBN = 128;          // key tokens per tile
-constexpr int kChunk = 128 * 128; // one 128-row x 128-byte swizzle-128B slab
-constexpr int kThreads = 192;
+constexpr int kBM = 128;           // rows of one tcgen05 M=128 tile
+constexpr int kQT = 2;             // query tiles per CTA
+constexpr int kBlockQ = kBM * kQT; // query rows per CTA (= CSR block_q)
+constexpr int kBN = 128;           // key tokens per tile (= CSR block_k)
+constexpr int kChunk = 128 * 128;  // one 128-row x 128-byte swizzle-128B slab
+constexpr int kSoftmaxWarps = 4 * kQT;
+constexpr int kProducerWarp = kSoftmaxWarps;
+constexpr int kMmaWarp = kSoftmaxWarps + 1;
+constexpr int kThreads = 32 * (kSoftmaxWarps + 2);
 constexpr uint32_t kTmemCols = 512;
 constexpr float kNegInf = -INFINITY;
+constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O only when the max grows by > 2^8
 
 struct AttnParams {
   void* o;
@@ -58,11 +64,11 @@ template <int D, int STAGES>
 struct Smem {
   static constexpr int kCh = D / 64;               // 128-byte column slabs per row
   static constexpr int kTile = kCh * kChunk;       // bytes of one 128 x D tile
-  static constexpr int kQ = 0;
-  static constexpr int kK = kTile;
+  static constexpr int kQ = 0;                     // kQT query tiles
+  static constexpr int kK = kQT * kTile;
   static constexpr int kV = kK + STAGES * kTile;
   static constexpr int kBar = kV + STAGES * kTile;
-  static constexpr int kNumBars = 1 + 3 * STAGES + 6 + 1;
+  static constexpr int kNumBars = 1 + 3 * STAGES + 3 * kQT + 1;
   static constexpr int kMisc = kBar + kNumBars * 8;
   static constexpr int kBytes = kMisc + 16 + 1024;  // + alignment slack
 };
@@ -88,6 +94,40 @@ __device__ __forceinline__ void set_cols(uint32_t (&am)[4], int a, int b) {  // 
   }
 }
 
+// Allowed-column mask of one key tile for one query row.
+__device__ __forceinline__ void tile_mask(uint32_t (&am)[4], const AttnParams& prm, int kt, bool text_row,
+                                          const uint32_t* fbits) {
+  am[0] = am[1] = am[2] = am[3] = 0u;
+  if (kt >= prm.nkv) {
+    set_cols(am, 0, min(kBN, prm.n_text - (kt - prm.nkv) * kBN));
+  } else if (text_row) {
+    set_cols(am, 0, min(kBN, prm.n_video - kt * kBN));
+  } else {
+    const int ks = kt * kBN, kend = min(ks + kBN, prm.n_video);
+    int f = ks / prm.P, c0 = 0;
+    while (ks + c0 < kend) {
+      const int ce = min((f + 1) * prm.P, kend) - ks;
+      if ((fbits[f >> 5] >> (f & 31)) & 1u) set_cols(am, c0, ce);
+      c0 = ce;
+      ++f;
+    }
+  }
+}
+
+// S_q(j) = Q_q K_j^T as two N=64 halves (keys 0-63 -> columns 0-63, keys
+// 64-127 -> columns 64-127).  The high half overwrites P_q(j-1), so it is
+// issued separately once PV_q(j-1) has completed.
+template <int D, bool kBf16>
+__device__ __forceinline__ void issue_s_half(uint32_t dS, uint32_t q_base, uint32_t k_base, int half) {
+  constexpr uint32_t idS = idesc_f16(kBM, 64, kBf16, false);
+#pragma unroll
+  for (int kk = 0; kk < D / 16; ++kk) {
+    const uint32_t off = (kk >> 2) * kChunk + (kk & 3) * 32;
+    mma_ss(dS + half * 64, sdesc_sw128(q_base + off, 16, 1024),
+           sdesc_sw128(k_base + half * 64 * 128 + off, 16, 1024), idS, kk > 0);
+  }
+}
+
 template <int D, int STAGES, bool kBf16>
 __global__ void __launch_bounds__(kThreads, 1)
     lvsa_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
@@ -105,10 +145,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* k_full = bars + 1;
   uint64_t* v_full = k_full + STAGES;
   uint64_t* kv_empty = v_full + STAGES;
-  uint64_t* s_full = kv_empty + STAGES;  // [2]
-  uint64_t* p_full = s_full + 2;         // [2]
-  uint64_t* pv_done = p_full + 2;        // [2]
-  uint64_t* drain = pv_done + 2;
+  uint64_t* s_full = kv_empty + STAGES;  // [kQT]
+  uint64_t* p_full = s_full + kQT;       // [kQT]
+  uint64_t* pv_done = p_full + kQT;      // [kQT]
+  uint64_t* drain = pv_done + kQT;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMisc);
   volatile int* abort = reinterpret_cast<volatile int*>(smem + L::kMisc + 4);
   volatile int* never = reinterpret_cast<volatile int*>(smem + L::kMisc + 8);  // stays 0: drain waits
@@ -118,7 +158,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int beg = prm.indptr[row];
   const int n = prm.indptr[row + 1] - beg;
   const bool text_row = row >= prm.nqv;
-  const int tok0 = (text_row ? row - prm.nqv : row) * kBM;
+  const int tok0 = (text_row ? row - prm.nqv : row) * kBlockQ;
   const int hk = h / (prm.heads / prm.kv_heads);
 
   if (threadIdx.x == 0) {
@@ -128,7 +168,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&v_full[s], 1);
       mbar_init(&kv_empty[s], 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kQT; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 128);
       mbar_init(&pv_done[i], 1);
@@ -138,7 +178,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     *never = 0;
     fence_mbar_init();
   }
-  if (warp == 5) {
+  if (warp == kMmaWarp) {
     tmem_alloc(tmem_slot, kTmemCols);
     tmem_relinquish();
   }
@@ -146,18 +186,23 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tS = tmem, tO = tmem + 256, tP = tmem + 384;
+  // TMEM columns: S_q [128q, 128q+128) (P_q in its upper 64), O_q [256 + Dq, 256 + D(q+1)).
+  auto tS = [&](int q) { return tmem + 128u * q; };
+  auto tO = [&](int q) { return tmem + 256u + static_cast<uint32_t>(D) * q; };
 
-  if (warp == 4) {
+  if (warp == kProducerWarp) {
     // ---------------------------------------------------------- producer
     if (lane == 0 && n > 0) {
       const CUtensorMap* mq = text_row ? &tm_tq : &tm_q;
       tma_prefetch_desc(mq);
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
-      mbar_expect_tx(q_full, L::kTile);
+      mbar_expect_tx(q_full, kQT * L::kTile);
 #pragma unroll
-      for (int c = 0; c < L::kCh; ++c) tma_load_4d(sQ + c * kChunk, mq, q_full, c * 64, h, tok0, b);
+      for (int q = 0; q < kQT; ++q)
+#pragma unroll
+        for (int c = 0; c < L::kCh; ++c)
+          tma_load_4d(sQ + q * L::kTile + c * kChunk, mq, q_full, c * 64, h, tok0 + q * kBM, b);
       int issued = 0;
       for (int j = 0; j < n; ++j) {
         const int s = j % STAGES;
@@ -188,38 +233,49 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == kMmaWarp) {
     // ---------------------------------------------------------- MMA issuer
+    // Per key tile j:  PV_0(j), S_0lo(j+1), [PV_0(j) done] S_0hi(j+1),
+    //                  PV_1(j), S_1lo(j+1), [PV_1(j) done] S_1hi(j+1).
+    // While softmax q works on S_q(j+1) the tensor pipe runs the other tile's
+    // PV and S (1024 of the 2048 MMA cycles per key tile).
     if (lane == 0 && n > 0) {
-      constexpr uint32_t idS = idesc_f16(kBM, kBN, kBf16, false);
       constexpr uint32_t idO = idesc_f16(kBM, D, kBf16, true);
       const uint32_t q_base = smem_u32(sQ), k_base = smem_u32(sK), v_base = smem_u32(sV);
-      if (mbar_wait(q_full, 0, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT)) {
-        for (int j = 0; j <= n; ++j) {
-          if (j < n) {
-            const int s = j % STAGES;
-            if (!mbar_wait(&k_full[s], (j / STAGES) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT)) break;
-            tc_fence_after();
-            const uint32_t dS = tS + (j & 1) * 128;
-            const uint32_t kb = k_base + s * L::kTile;
+      bool ok = mbar_wait(q_full, 0, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT) &&
+                mbar_wait(&k_full[0], 0, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT);
+      if (ok) {
+        tc_fence_after();
 #pragma unroll
-            for (int kk = 0; kk < D / 16; ++kk) {
-              const uint32_t off = (kk >> 2) * kChunk + (kk & 3) * 32;
-              mma_ss(dS, sdesc_sw128(q_base + off, 16, 1024), sdesc_sw128(kb + off, 16, 1024), idS, kk > 0);
-            }
-            mma_commit(&s_full[j & 1]);
-          }
-          if (j > 0) {
-            const int jj = j - 1, bb = jj & 1, s = jj % STAGES;
-            if (!mbar_wait(&p_full[bb], (jj >> 1) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT)) break;
-            if (!mbar_wait(&v_full[s], (jj / STAGES) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT)) break;
-            tc_fence_after();
-            const uint32_t vb = v_base + s * L::kTile;
+        for (int q = 0; q < kQT; ++q) {
+          issue_s_half<D, kBf16>(tS(q), q_base + q * L::kTile, k_base, 0);
+          issue_s_half<D, kBf16>(tS(q), q_base + q * L::kTile, k_base, 1);
+          mma_commit(&s_full[q]);
+        }
+      }
+      for (int j = 0; ok && j < n; ++j) {
+        const int st = j % STAGES, st1 = (j + 1) % STAGES;
+        const bool has_next = j + 1 < n;
+        if (!mbar_wait(&v_full[st], (j / STAGES) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT)) break;
+        if (has_next && !mbar_wait(&k_full[st1], ((j + 1) / STAGES) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT))
+          break;
+        const uint32_t vb = v_base + st * L::kTile, kb1 = k_base + st1 * L::kTile;
 #pragma unroll
-            for (int kk = 0; kk < kBN / 16; ++kk)
-              mma_ts(tO, tP + bb * 64 + kk * 8, sdesc_sw128(vb + kk * 2048, kChunk, 1024), idO, (jj > 0 || kk > 0));
-            mma_commit(&pv_done[bb]);
-            mma_commit(&kv_empty[s]);
+        for (int q = 0; q < kQT; ++q) {
+          if (!(ok = mbar_wait(&p_full[q], j & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT))) break;
+          tc_fence_after();
+          const uint32_t tP = tS(q) + 64;
+#pragma unroll
+          for (int kk = 0; kk < kBN / 16; ++kk)
+            mma_ts(tO(q), tP + kk * 8, sdesc_sw128(vb + kk * 2048, kChunk, 1024), idO, (j > 0 || kk > 0));
+          mma_commit(&pv_done[q]);
+          if (q == kQT - 1) mma_commit(&kv_empty[st]);
+          if (has_next) {
+            issue_s_half<D, kBf16>(tS(q), q_base + q * L::kTile, kb1, 0);
+            if (!(ok = mbar_wait(&pv_done[q], j & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT))) break;
+            tc_fence_after();
+            issue_s_half<D, kBf16>(tS(q), q_base + q * L::kTile, kb1, 1);
+            mma_commit(&s_full[q]);
           }
         }
       }
@@ -229,100 +285,81 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ---------------------------------------------------------- softmax
-    const int r = threadIdx.x;
+    const int q = warp >> 2;                     // query tile of this warpgroup
+    const int r = threadIdx.x & (kBM - 1);       // row in the tile = TMEM lane
     const int seg_len = text_row ? prm.n_text : prm.n_video;
-    const int tok = tok0 + r;
+    const int tok = tok0 + q * kBM + r;
     const bool valid = tok < seg_len;
     const int fq = text_row ? 0 : min(tok / prm.P, prm.T - 1);
     const uint32_t* fbits = prm.frame_bits + static_cast<size_t>(fq) * prm.words;
-    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t tSq = tS(q) + lane_base, tPq = tSq + 64, tOq = tO(q) + lane_base;
     const float sl2 = prm.scale_log2;
     float m = kNegInf, l = 0.f;
     bool ok = true;
+    int flag_next = n > 0 ? prm.flags[beg] : 0;
+    int kt_next = n > 0 ? prm.indices[beg] : 0;
     for (int j = 0; j < n; ++j) {
-      const int bb = j & 1;
-      ok = __all_sync(0xFFFFFFFFu, mbar_wait(&s_full[bb], (j >> 1) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT));
+      const int flag = flag_next, kt = kt_next;
+      if (j + 1 < n) {
+        flag_next = prm.flags[beg + j + 1];
+        kt_next = prm.indices[beg + j + 1];
+      }
+      ok = __all_sync(0xFFFFFFFFu, mbar_wait(&s_full[q], j & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT));
       if (!ok) break;
       tc_fence_after();
-      float s[kBN];
-#pragma unroll
-      for (int c = 0; c < kBN / 32; ++c) {
-        uint32_t t[32];
-        tmem_ld32(tS + lane_base + bb * 128 + c * 32, t);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(t[i]);
-      }
-      if (prm.flags[beg + j]) {
-        uint32_t am[4] = {0u, 0u, 0u, 0u};
-        const int kt = prm.indices[beg + j];
-        if (kt >= prm.nkv) {
-          set_cols(am, 0, min(kBN, prm.n_text - (kt - prm.nkv) * kBN));
-        } else if (text_row) {
-          set_cols(am, 0, min(kBN, prm.n_video - kt * kBN));
-        } else {
-          const int ks = kt * kBN, kend = min(ks + kBN, prm.n_video);
-          int f = ks / prm.P, c0 = 0;
-          while (ks + c0 < kend) {
-            const int ce = min((f + 1) * prm.P, kend) - ks;
-            if ((fbits[f >> 5] >> (f & 31)) & 1u) set_cols(am, c0, ce);
-            c0 = ce;
-            ++f;
-          }
-        }
+      uint32_t s[kBN];
+      tmem_ld128(tSq, s);
+      if (flag) {
+        uint32_t am[4];
+        tile_mask(am, prm, kt, text_row, fbits);
 #pragma unroll
         for (int i = 0; i < kBN; ++i)
-          if (!((am[i >> 5] >> (i & 31)) & 1u)) s[i] = kNegInf;
+          if (!((am[i >> 5] >> (i & 31)) & 1u)) s[i] = __float_as_uint(kNegInf);
       }
-      float mx = s[0];
+      float mx8[8];
 #pragma unroll
-      for (int i = 1; i < kBN; ++i) mx = fmaxf(mx, s[i]);
+      for (int i = 0; i < 8; ++i) mx8[i] = __uint_as_float(s[i]);
+#pragma unroll
+      for (int i = 8; i < kBN; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], __uint_as_float(s[i]));
+      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
       const float m_new = fmaxf(m, mx * sl2);
       if (j == 0) {
         m = m_new;
       } else {
-        const bool need = m_new > m + 8.0f;
+        // Lazy rescale: O_q is quiescent here (PV_q(j-1) completed before S_q(j) was issued).
+        const bool need = m_new > m + kRescaleThreshold;
         if (__any_sync(0xFFFFFFFFu, need)) {
           const float alpha = need ? ex2_approx(m - m_new) : 1.f;
           if (need) m = m_new;
-          ok = __all_sync(0xFFFFFFFFu, mbar_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, abort, prm.err,
-                                                 LVSA_ERR_DEVICE_TIMEOUT));
-          if (!ok) break;
-          tc_fence_after();
 #pragma unroll
           for (int c = 0; c < D / 32; ++c) {
             uint32_t t[32];
-            tmem_ld32(tO + lane_base + c * 32, t);
+            tmem_ld32(tOq + c * 32, t);
 #pragma unroll
             for (int i = 0; i < 32; ++i) t[i] = __float_as_uint(__uint_as_float(t[i]) * alpha);
-            tmem_st32(tO + lane_base + c * 32, t);
+            tmem_st32(tOq + c * 32, t);
           }
           l *= alpha;
         }
       }
       const float mu = (m == kNegInf) ? 0.f : m;
-      float sum = 0.f;
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      uint32_t pk[kBN / 2];
 #pragma unroll
-      for (int i = 0; i < kBN; ++i) {
-        s[i] = ex2_approx(fmaf(s[i], sl2, -mu));
-        sum += s[i];
+      for (int i = 0; i < kBN / 2; ++i) {
+        const float a = ex2_approx(fmaf(__uint_as_float(s[2 * i]), sl2, -mu));
+        const float c = ex2_approx(fmaf(__uint_as_float(s[2 * i + 1]), sl2, -mu));
+        acc[(2 * i) & 7] += a;
+        acc[(2 * i + 1) & 7] += c;
+        pk[i] = pack2(a, c, kBf16);
       }
-      l += sum;
-      if (j >= 2) {
-        ok = __all_sync(0xFFFFFFFFu, mbar_wait(&pv_done[bb], ((j - 2) >> 1) & 1, abort, prm.err,
-                                               LVSA_ERR_DEVICE_TIMEOUT));
-        if (!ok) break;
-        tc_fence_after();
-      }
-#pragma unroll
-      for (int hcol = 0; hcol < 2; ++hcol) {
-        uint32_t pk[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) pk[i] = pack2(s[hcol * 64 + 2 * i], s[hcol * 64 + 2 * i + 1], kBf16);
-        tmem_st32(tP + lane_base + bb * 64 + hcol * 32, pk);
-      }
+      l += ((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7]));
+      tmem_st64(tPq, pk);
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&p_full[bb]);
+      mbar_arrive(&p_full[q]);
     }
     // ---------------------------------------------------------- epilogue
     using Elem = typename std::conditional<kBf16, __nv_bfloat16, __half>::type;
@@ -338,15 +375,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (prm.lse) lse = prm.lse + (static_cast<int64_t>(b) * prm.heads + h) * prm.n_video + tok;
     }
     if (ok && n > 0) {
-      ok = __all_sync(0xFFFFFFFFu, mbar_wait(&pv_done[(n - 1) & 1], ((n - 1) >> 1) & 1, abort, prm.err,
-                                             LVSA_ERR_DEVICE_TIMEOUT));
+      ok = __all_sync(0xFFFFFFFFu, mbar_wait(&pv_done[q], (n - 1) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT));
       if (ok) {
         tc_fence_after();
         const float inv = (l > 0.f) ? 1.f / l : 0.f;
 #pragma unroll
         for (int c = 0; c < D / 32; ++c) {
           uint32_t t[32];
-          tmem_ld32(tO + lane_base + c * 32, t);
+          tmem_ld32(tOq + c * 32, t);
           if (valid && obase) {
             uint32_t pk[16];
 #pragma unroll
@@ -371,7 +407,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
@@ -474,22 +510,22 @@ extern "C" int lvsa_attn_fwd(const LvsaAttnArgs* a, void* stream) {
   if (a->batch < 1 || a->n_video < 1 || a->n_text < 0 || a->heads < 1 || a->kv_heads < 1 ||
       a->heads % a->kv_heads)
     return LVSA_ERR_INVALID_ARG;
-  if (a->block_q != kBM || a->block_k != kBN) return LVSA_ERR_UNSUPPORTED;
+  if (a->block_q != kBlockQ || a->block_k != kBN) return LVSA_ERR_UNSUPPORTED;
   if (a->total_frames < 1 || a->num_patches < 1 ||
       static_cast<long long>(a->total_frames) * a->num_patches != a->n_video)
     return LVSA_ERR_GEOMETRY;
-  if (a->n_q_video_tiles != (a->n_video + kBM - 1) / kBM || a->n_k_video_tiles != (a->n_video + kBN - 1) / kBN ||
+  if (a->n_q_video_tiles != (a->n_video + kBlockQ - 1) / kBlockQ || a->n_k_video_tiles != (a->n_video + kBN - 1) / kBN ||
       a->frame_words != (a->total_frames + 31) / 32)
     return LVSA_ERR_GEOMETRY;
   if (a->n_text > 0 && (!a->text_k.ptr || !a->text_v.ptr)) return LVSA_ERR_INVALID_ARG;
   if (a->n_text > 0 && a->text_q.ptr && !a->text_o.ptr) return LVSA_ERR_INVALID_ARG;
-  if (a->n_text > 0 && a->n_q_tiles != a->n_q_video_tiles + (a->n_text + kBM - 1) / kBM) return LVSA_ERR_GEOMETRY;
+  if (a->n_text > 0 && a->n_q_tiles != a->n_q_video_tiles + (a->n_text + kBlockQ - 1) / kBlockQ) return LVSA_ERR_GEOMETRY;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool bf16 = a->dtype == LVSA_DTYPE_BF16;
   if (a->dtype != LVSA_DTYPE_BF16 && a->dtype != LVSA_DTYPE_F16) return LVSA_ERR_UNSUPPORTED;
   switch (a->head_dim) {
     case 128: return bf16 ? launch<128, 2, true>(a, s) : launch<128, 2, false>(a, s);
-    case 64: return bf16 ? launch<64, 4, true>(a, s) : launch<64, 4, false>(a, s);
+    case 64: return bf16 ? launch<64, 5, true>(a, s) : launch<64, 5, false>(a, s);
     default: return LVSA_ERR_UNSUPPORTED;
   }
 }

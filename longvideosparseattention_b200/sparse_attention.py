@@ -20,7 +20,7 @@ from typing import Any, Dict, List, Optional, Sequence, Set, Tuple
 
 import torch
 
-from .block_sparse import BlockMask, block_sparse_attention, build_block_mask
+from .block_sparse import ATTN_BLOCK_K, ATTN_BLOCK_Q, BlockMask, block_sparse_attention, build_block_mask
 
 # --------------------------------------------------------------------------
 # Pattern helpers
@@ -291,8 +291,8 @@ class LVSAMetadata:
         lo, hi = (int(x) for x in self.window_bounds[f].tolist())
         return sorted(self.global_set | set(range(lo, hi + 1)))
 
-    def block_mask(self, device: torch.device, n_text: int = 0, block_q: int = 128,
-                   block_k: int = 128) -> BlockMask:
+    def block_mask(self, device: torch.device, n_text: int = 0, block_q: int = ATTN_BLOCK_Q,
+                   block_k: int = ATTN_BLOCK_K) -> BlockMask:
         """GPU tile CSR of this pattern (world = 1 semantics), cached per device."""
         device = torch.device(device)
         key = (str(device), int(n_text), block_q, block_k)

@@ -100,7 +100,7 @@ def test_mask_buffer_reuse_across_steps():
         m2 = build_block_mask(81, 1560, 2, 1, 4, step % 4, reuse=m, device="cuda")
         assert m2.tile_indices.data_ptr() == m.tile_indices.data_ptr()
         fp = O.frame_pattern(81, 1560, 2, 1, 4, step % 4)
-        wi, wx, wf, _, _ = O.tile_csr(fp["attended"], 81, 1560, 81 * 1560)
+        wi, wx, wf, _, _ = O.tile_csr(fp["attended"], 81, 1560, 81 * 1560, 0, m.block_q, m.block_k)
         indptr, idx, fl = m2.host_csr()
         np.testing.assert_array_equal(idx.numpy(), wx)
         np.testing.assert_array_equal(fl.numpy(), wf)

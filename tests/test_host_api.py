@@ -158,7 +158,7 @@ int main(void){
 def test_mask_layout_host_call_and_errors():
     from longvideosparseattention_b200 import mask_layout
     from longvideosparseattention_b200 import _native as N
-    _, lay, _ = mask_layout(81, 1560, 2, 1, 4, 0, True, 0)
+    _, lay, _ = mask_layout(81, 1560, 2, 1, 4, 0, True, 0, 128, 128)
     assert (lay.n_video, lay.n_q_video_tiles, lay.n_k_video_tiles, lay.frame_words) == (126360, 988, 988, 3)
     fp = O.frame_pattern(81, 1560, 2, 1, 4, 0)
     _, idx, _, _, _ = O.tile_csr(fp["attended"], 81, 1560, 126360)
