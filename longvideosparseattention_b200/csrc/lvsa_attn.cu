@@ -308,20 +308,36 @@ __global__ void __launch_bounds__(kThreads, 1)
       ok = __all_sync(0xFFFFFFFFu, mbar_wait(&s_full[q], j & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT));
       if (!ok) break;
       tc_fence_after();
-      uint32_t s[kBN];
-      tmem_ld128(tSq, s);
-      if (flag) {
-        uint32_t am[4];
-        tile_mask(am, prm, kt, text_row, fbits);
-#pragma unroll
-        for (int i = 0; i < kBN; ++i)
-          if (!((am[i >> 5] >> (i & 31)) & 1u)) s[i] = __float_as_uint(kNegInf);
-      }
+      // Half a row at a time keeps ~130 registers live (no spills at the
+      // 168-register cap of 320 threads): the low half (keys 0-63) is read
+      // once for its max and again for its exponentials; the high half stays
+      // in registers.  P (keys 0-63 -> columns 64-95, keys 64-127 -> 96-127)
+      // only overwrites S columns already consumed.
+      uint32_t am[4] = {~0u, ~0u, ~0u, ~0u};
+      if (flag) tile_mask(am, prm, kt, text_row, fbits);
       float mx8[8];
+      {
+        uint32_t lo[64];
+        tmem_ld64(tSq, lo);
+        if (flag) {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) mx8[i] = __uint_as_float(s[i]);
+          for (int i = 0; i < 64; ++i)
+            if (!((am[i >> 5] >> (i & 31)) & 1u)) lo[i] = __float_as_uint(kNegInf);
+        }
 #pragma unroll
-      for (int i = 8; i < kBN; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], __uint_as_float(s[i]));
+        for (int i = 0; i < 8; ++i) mx8[i] = __uint_as_float(lo[i]);
+#pragma unroll
+        for (int i = 8; i < 64; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], __uint_as_float(lo[i]));
+      }
+      uint32_t hi[64];
+      tmem_ld64(tSq + 64, hi);
+      if (flag) {
+#pragma unroll
+        for (int i = 0; i < 64; ++i)
+          if (!((am[2 + (i >> 5)] >> (i & 31)) & 1u)) hi[i] = __float_as_uint(kNegInf);
+      }
+#pragma unroll
+      for (int i = 0; i < 64; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], __uint_as_float(hi[i]));
       const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
                              fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
       const float m_new = fmaxf(m, mx * sl2);
@@ -346,17 +362,38 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const float mu = (m == kNegInf) ? 0.f : m;
       float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      uint32_t pk[kBN / 2];
+      {
+        uint32_t pk[32];
 #pragma unroll
-      for (int i = 0; i < kBN / 2; ++i) {
-        const float a = ex2_approx(fmaf(__uint_as_float(s[2 * i]), sl2, -mu));
-        const float c = ex2_approx(fmaf(__uint_as_float(s[2 * i + 1]), sl2, -mu));
-        acc[(2 * i) & 7] += a;
-        acc[(2 * i + 1) & 7] += c;
-        pk[i] = pack2(a, c, kBf16);
+        for (int i = 0; i < 32; ++i) {
+          const float a = ex2_approx(fmaf(__uint_as_float(hi[2 * i]), sl2, -mu));
+          const float c = ex2_approx(fmaf(__uint_as_float(hi[2 * i + 1]), sl2, -mu));
+          acc[(2 * i) & 7] += a;
+          acc[(2 * i + 1) & 7] += c;
+          pk[i] = pack2(a, c, kBf16);
+        }
+        tmem_st32(tPq + 32, pk);
+      }
+      {
+        uint32_t lo[64];
+        tmem_ld64(tSq, lo);
+        if (flag) {
+#pragma unroll
+          for (int i = 0; i < 64; ++i)
+            if (!((am[i >> 5] >> (i & 31)) & 1u)) lo[i] = __float_as_uint(kNegInf);
+        }
+        uint32_t pk[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float a = ex2_approx(fmaf(__uint_as_float(lo[2 * i]), sl2, -mu));
+          const float c = ex2_approx(fmaf(__uint_as_float(lo[2 * i + 1]), sl2, -mu));
+          acc[(2 * i) & 7] += a;
+          acc[(2 * i + 1) & 7] += c;
+          pk[i] = pack2(a, c, kBf16);
+        }
+        tmem_st32(tPq, pk);
       }
       l += ((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7]));
-      tmem_st64(tPq, pk);
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&p_full[q]);
