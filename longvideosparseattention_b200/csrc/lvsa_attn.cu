@@ -43,6 +43,11 @@ constexpr int kMmaWarp = kSoftmaxWarps + 1;
 constexpr int kThreads = 32 * (kSoftmaxWarps + 2);
 constexpr uint32_t kTmemCols = 512;
 constexpr float kNegInf = -INFINITY;
+#ifndef LVSA_EMU
+#define LVSA_EMU 0
+#endif
+// Exponentials per 8 evaluated by polynomial on the FMA pipe.
+constexpr int kEmuPer8 = LVSA_EMU;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O only when the max grows by > 2^8
 
 struct AttnParams {
@@ -68,7 +73,7 @@ struct Smem {
   static constexpr int kK = kQT * kTile;
   static constexpr int kV = kK + STAGES * kTile;
   static constexpr int kBar = kV + STAGES * kTile;
-  static constexpr int kNumBars = 1 + 3 * STAGES + 3 * kQT + 1;
+  static constexpr int kNumBars = 1 + 4 * STAGES + 3 * kQT + 1;
   static constexpr int kMisc = kBar + kNumBars * 8;
   static constexpr int kBytes = kMisc + 16 + 1024;  // + alignment slack
 };
@@ -144,8 +149,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;
   uint64_t* v_full = k_full + STAGES;
-  uint64_t* kv_empty = v_full + STAGES;
-  uint64_t* s_full = kv_empty + STAGES;  // [kQT]
+  uint64_t* k_empty = v_full + STAGES;   // K stage free: every S of its tile done
+  uint64_t* v_empty = k_empty + STAGES;  // V stage free: every PV of its tile done
+  uint64_t* s_full = v_empty + STAGES;   // [kQT]
   uint64_t* p_full = s_full + kQT;       // [kQT]
   uint64_t* pv_done = p_full + kQT;      // [kQT]
   uint64_t* drain = pv_done + kQT;
@@ -166,7 +172,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&v_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_empty[s], 1);
     }
     for (int i = 0; i < kQT; ++i) {
       mbar_init(&s_full[i], 1);
@@ -206,7 +213,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int issued = 0;
       for (int j = 0; j < n; ++j) {
         const int s = j % STAGES;
-        if (j >= STAGES && !mbar_wait(&kv_empty[s], ((j / STAGES) - 1) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT))
+        if (j >= STAGES && !mbar_wait(&k_empty[s], ((j / STAGES) - 1) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT))
           break;
         const int kt = prm.indices[beg + j];
         const bool tt = kt >= prm.nkv;
@@ -217,6 +224,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int c = 0; c < L::kCh; ++c)
           tma_load_4d(sK + s * L::kTile + c * kChunk, mk, &k_full[s], c * 64, hk, ktok, b);
+        // K and V stages are released separately: K as soon as both S MMAs
+        // of its tile are done, V after both PVs, so the next K is in flight
+        // a full PV phase earlier.
+        if (j >= STAGES && !mbar_wait(&v_empty[s], ((j / STAGES) - 1) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT))
+          break;
         mbar_expect_tx(&v_full[s], L::kTile);
 #pragma unroll
         for (int c = 0; c < L::kCh; ++c)
@@ -252,6 +264,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           issue_s_half<D, kBf16>(tS(q), q_base + q * L::kTile, k_base, 1);
           mma_commit(&s_full[q]);
         }
+        mma_commit(&k_empty[0]);
       }
       for (int j = 0; ok && j < n; ++j) {
         const int st = j % STAGES, st1 = (j + 1) % STAGES;
@@ -269,13 +282,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int kk = 0; kk < kBN / 16; ++kk)
             mma_ts(tO(q), tP + kk * 8, sdesc_sw128(vb + kk * 2048, kChunk, 1024), idO, (j > 0 || kk > 0));
           mma_commit(&pv_done[q]);
-          if (q == kQT - 1) mma_commit(&kv_empty[st]);
+          if (q == kQT - 1) mma_commit(&v_empty[st]);
           if (has_next) {
             issue_s_half<D, kBf16>(tS(q), q_base + q * L::kTile, kb1, 0);
             if (!(ok = mbar_wait(&pv_done[q], j & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT))) break;
             tc_fence_after();
             issue_s_half<D, kBf16>(tS(q), q_base + q * L::kTile, kb1, 1);
             mma_commit(&s_full[q]);
+            if (q == kQT - 1) mma_commit(&k_empty[st1]);
           }
         }
       }
@@ -308,38 +322,37 @@ __global__ void __launch_bounds__(kThreads, 1)
       ok = __all_sync(0xFFFFFFFFu, mbar_wait(&s_full[q], j & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT));
       if (!ok) break;
       tc_fence_after();
-      // Half a row at a time keeps ~130 registers live (no spills at the
-      // 168-register cap of 320 threads): the low half (keys 0-63) is read
-      // once for its max and again for its exponentials; the high half stays
-      // in registers.  P (keys 0-63 -> columns 64-95, keys 64-127 -> 96-127)
-      // only overwrites S columns already consumed.
+      // Both 64-column halves of the S row are loaded under one wait; P
+      // (keys 0-63 -> columns 64-95, keys 64-127 -> 96-127) then only
+      // overwrites S columns already held in registers.
       uint32_t am[4] = {~0u, ~0u, ~0u, ~0u};
       if (flag) tile_mask(am, prm, kt, text_row, fbits);
-      float mx8[8];
-      {
-        uint32_t lo[64];
-        tmem_ld64(tSq, lo);
-        if (flag) {
-#pragma unroll
-          for (int i = 0; i < 64; ++i)
-            if (!((am[i >> 5] >> (i & 31)) & 1u)) lo[i] = __float_as_uint(kNegInf);
-        }
-#pragma unroll
-        for (int i = 0; i < 8; ++i) mx8[i] = __uint_as_float(lo[i]);
-#pragma unroll
-        for (int i = 8; i < 64; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], __uint_as_float(lo[i]));
-      }
-      uint32_t hi[64];
-      tmem_ld64(tSq + 64, hi);
+      uint32_t lo[64], hi[64];
+      tmem_ld64x2(tSq, tSq + 64, lo, hi);
       if (flag) {
 #pragma unroll
-        for (int i = 0; i < 64; ++i)
+        for (int i = 0; i < 64; ++i) {
+          if (!((am[i >> 5] >> (i & 31)) & 1u)) lo[i] = __float_as_uint(kNegInf);
           if (!((am[2 + (i >> 5)] >> (i & 31)) & 1u)) hi[i] = __float_as_uint(kNegInf);
+        }
+      }
+      // 16 independent max chains (dependency depth 8 instead of 16).
+      float mx16[16];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        mx16[i] = __uint_as_float(lo[i]);
+        mx16[8 + i] = __uint_as_float(hi[i]);
       }
 #pragma unroll
-      for (int i = 0; i < 64; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], __uint_as_float(hi[i]));
-      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+      for (int i = 8; i < 64; ++i) {
+        mx16[i & 7] = fmaxf(mx16[i & 7], __uint_as_float(lo[i]));
+        mx16[8 + (i & 7)] = fmaxf(mx16[8 + (i & 7)], __uint_as_float(hi[i]));
+      }
+#pragma unroll
+      for (int w = 8; w >= 1; w >>= 1)
+#pragma unroll
+        for (int i = 0; i < w; ++i) mx16[i] = fmaxf(mx16[i], mx16[i + w]);
+      const float mx = mx16[0];
       const float m_new = fmaxf(m, mx * sl2);
       if (j == 0) {
         m = m_new;
@@ -361,38 +374,35 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       const float mu = (m == kNegInf) ? 0.f : m;
-      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      {
+      // Packed fp32x2: argument (s*scale - m) and the row sum run two lanes
+      // per instruction; kEmuPer8 of every 8 exponentials use ex2_poly2 on
+      // the FMA pipe, the rest MUFU.
+      const uint64_t sl2x2 = f2_pack(sl2, sl2), nmu2 = f2_pack(-mu, -mu);
+      uint64_t acc2[4] = {0ull, 0ull, 0ull, 0ull};
+#pragma unroll
+      for (int hc = 0; hc < 2; ++hc) {
+        const uint32_t* sv = hc ? hi : lo;
         uint32_t pk[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          const float a = ex2_approx(fmaf(__uint_as_float(hi[2 * i]), sl2, -mu));
-          const float c = ex2_approx(fmaf(__uint_as_float(hi[2 * i + 1]), sl2, -mu));
-          acc[(2 * i) & 7] += a;
-          acc[(2 * i + 1) & 7] += c;
+          const int e = 2 * i;
+          const uint64_t x2 = f2_fma(f2_pack(__uint_as_float(sv[e]), __uint_as_float(sv[e + 1])), sl2x2, nmu2);
+          float xa, xc, a, c;
+          f2_unpack(x2, xa, xc);
+          if ((e & 7) < kEmuPer8) {
+            ex2_poly2(xa, xc, a, c);
+          } else {
+            a = ex2_approx(xa);
+            c = ex2_approx(xc);
+          }
+          acc2[i & 3] = f2_add(acc2[i & 3], f2_pack(a, c));
           pk[i] = pack2(a, c, kBf16);
         }
-        tmem_st32(tPq + 32, pk);
+        tmem_st32(tPq + hc * 32, pk);
       }
-      {
-        uint32_t lo[64];
-        tmem_ld64(tSq, lo);
-        if (flag) {
+      float acc[8];
 #pragma unroll
-          for (int i = 0; i < 64; ++i)
-            if (!((am[i >> 5] >> (i & 31)) & 1u)) lo[i] = __float_as_uint(kNegInf);
-        }
-        uint32_t pk[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float a = ex2_approx(fmaf(__uint_as_float(lo[2 * i]), sl2, -mu));
-          const float c = ex2_approx(fmaf(__uint_as_float(lo[2 * i + 1]), sl2, -mu));
-          acc[(2 * i) & 7] += a;
-          acc[(2 * i + 1) & 7] += c;
-          pk[i] = pack2(a, c, kBf16);
-        }
-        tmem_st32(tPq, pk);
-      }
+      for (int i = 0; i < 4; ++i) f2_unpack(acc2[i], acc[2 * i], acc[2 * i + 1]);
       l += ((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7]));
       tmem_wait_st();
       tc_fence_before();

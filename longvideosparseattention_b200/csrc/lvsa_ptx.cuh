@@ -46,6 +46,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking probe of a phase (never suspends the thread).
+__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Every wait is bounded: after `timeout_ns` (or once another thread of the
 // CTA raised `abort`) it gives up, records `code` in the device error word and
 // returns false, so a logic error can never hang the GPU.
@@ -189,6 +202,16 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
                :: "r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
                : "memory");
 }
+// Two 64-column TMEM loads in flight together, one completion wait.
+__device__ __forceinline__ void tmem_ld64x2(uint32_t ta, uint32_t tb, uint32_t (&a)[64], uint32_t (&b)[64]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%128];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x64.b32 {%64,%65,%66,%67,%68,%69,%70,%71,%72,%73,%74,%75,%76,%77,%78,%79,%80,%81,%82,%83,%84,%85,%86,%87,%88,%89,%90,%91,%92,%93,%94,%95,%96,%97,%98,%99,%100,%101,%102,%103,%104,%105,%106,%107,%108,%109,%110,%111,%112,%113,%114,%115,%116,%117,%118,%119,%120,%121,%122,%123,%124,%125,%126,%127}, [%129];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3]), "=r"(a[4]), "=r"(a[5]), "=r"(a[6]), "=r"(a[7]), "=r"(a[8]), "=r"(a[9]), "=r"(a[10]), "=r"(a[11]), "=r"(a[12]), "=r"(a[13]), "=r"(a[14]), "=r"(a[15]), "=r"(a[16]), "=r"(a[17]), "=r"(a[18]), "=r"(a[19]), "=r"(a[20]), "=r"(a[21]), "=r"(a[22]), "=r"(a[23]), "=r"(a[24]), "=r"(a[25]), "=r"(a[26]), "=r"(a[27]), "=r"(a[28]), "=r"(a[29]), "=r"(a[30]), "=r"(a[31]), "=r"(a[32]), "=r"(a[33]), "=r"(a[34]), "=r"(a[35]), "=r"(a[36]), "=r"(a[37]), "=r"(a[38]), "=r"(a[39]), "=r"(a[40]), "=r"(a[41]), "=r"(a[42]), "=r"(a[43]), "=r"(a[44]), "=r"(a[45]), "=r"(a[46]), "=r"(a[47]), "=r"(a[48]), "=r"(a[49]), "=r"(a[50]), "=r"(a[51]), "=r"(a[52]), "=r"(a[53]), "=r"(a[54]), "=r"(a[55]), "=r"(a[56]), "=r"(a[57]), "=r"(a[58]), "=r"(a[59]), "=r"(a[60]), "=r"(a[61]), "=r"(a[62]), "=r"(a[63]), "=r"(b[0]), "=r"(b[1]), "=r"(b[2]), "=r"(b[3]), "=r"(b[4]), "=r"(b[5]), "=r"(b[6]), "=r"(b[7]), "=r"(b[8]), "=r"(b[9]), "=r"(b[10]), "=r"(b[11]), "=r"(b[12]), "=r"(b[13]), "=r"(b[14]), "=r"(b[15]), "=r"(b[16]), "=r"(b[17]), "=r"(b[18]), "=r"(b[19]), "=r"(b[20]), "=r"(b[21]), "=r"(b[22]), "=r"(b[23]), "=r"(b[24]), "=r"(b[25]), "=r"(b[26]), "=r"(b[27]), "=r"(b[28]), "=r"(b[29]), "=r"(b[30]), "=r"(b[31]), "=r"(b[32]), "=r"(b[33]), "=r"(b[34]), "=r"(b[35]), "=r"(b[36]), "=r"(b[37]), "=r"(b[38]), "=r"(b[39]), "=r"(b[40]), "=r"(b[41]), "=r"(b[42]), "=r"(b[43]), "=r"(b[44]), "=r"(b[45]), "=r"(b[46]), "=r"(b[47]), "=r"(b[48]), "=r"(b[49]), "=r"(b[50]), "=r"(b[51]), "=r"(b[52]), "=r"(b[53]), "=r"(b[54]), "=r"(b[55]), "=r"(b[56]), "=r"(b[57]), "=r"(b[58]), "=r"(b[59]), "=r"(b[60]), "=r"(b[61]), "=r"(b[62]), "=r"(b[63])
+      : "r"(ta), "r"(tb)
+      : "memory");
+}
 __device__ __forceinline__ void tmem_wait_st() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
@@ -219,6 +242,74 @@ __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// 2^x evaluated on the FMA/ALU pipes instead of the MUFU unit, for the
+// softmax arguments x <= ~8.  Range reduction: j = round(x) by adding
+// 1.5 * 2^23 (fp32 round-to-nearest leaves j in the low mantissa bits),
+// f = x - j in [-0.5, 0.5]; 2^f by a degree-3 polynomial whose coefficients
+// were fitted here for minimax relative error on [-0.5, 0.5] with Lawson's
+// iteratively reweighted least squares (max relative error 7.5e-5, far below
+// the 2^-9 of the bf16 P it feeds); 2^j is added into the exponent field.
+// x below -126 (including -inf from the mask) returns exactly 0.
+__device__ __forceinline__ float ex2_poly(float x) {
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+  constexpr int kRoundBits = 0x4B400000;
+  const float xc = fmaxf(x, -126.0f);
+  const float t = xc + kRound;
+  const float f = xc - (t - kRound);
+  float p = fmaf(0.05517167f, f, 0.24261114f);
+  p = fmaf(p, f, 0.69326099f);
+  p = fmaf(p, f, 0.99992807f);
+  const int j = __float_as_int(t) - kRoundBits;
+  const float y = __int_as_float(__float_as_int(p) + (j << 23));
+  return x < -126.0f ? 0.0f : y;
+}
+
+// ---------------------------------------------------------------- f32x2
+// Blackwell packed-fp32 arithmetic: one instruction on two lanes of a
+// 64-bit register pair.
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// ex2_poly on two lanes at once (same method and coefficients), using the
+// packed FMA/add for the arithmetic part.
+__device__ __forceinline__ void ex2_poly2(float x0, float x1, float& y0, float& y1) {
+  constexpr float kRound = 12582912.0f;
+  constexpr int kRoundBits = 0x4B400000;
+  const float c0 = fmaxf(x0, -126.0f), c1 = fmaxf(x1, -126.0f);
+  const uint64_t xc = f2_pack(c0, c1);
+  const uint64_t rb = f2_pack(kRound, kRound), nrb = f2_pack(-kRound, -kRound);
+  const uint64_t t = f2_add(xc, rb);
+  const uint64_t jf = f2_add(t, nrb);
+  float j0, j1, t0, t1;
+  f2_unpack(jf, j0, j1);
+  f2_unpack(t, t0, t1);
+  const uint64_t f = f2_add(xc, f2_pack(-j0, -j1));
+  uint64_t p = f2_fma(f2_pack(0.05517167f, 0.05517167f), f, f2_pack(0.24261114f, 0.24261114f));
+  p = f2_fma(p, f, f2_pack(0.69326099f, 0.69326099f));
+  p = f2_fma(p, f, f2_pack(0.99992807f, 0.99992807f));
+  float p0, p1;
+  f2_unpack(p, p0, p1);
+  const int e0 = __float_as_int(t0) - kRoundBits, e1 = __float_as_int(t1) - kRoundBits;
+  y0 = x0 < -126.0f ? 0.0f : __int_as_float(__float_as_int(p0) + (e0 << 23));
+  y1 = x1 < -126.0f ? 0.0f : __int_as_float(__float_as_int(p1) + (e1 << 23));
 }
 
 }  // namespace lvsa
