@@ -19,10 +19,10 @@ from . import _native as N
 
 _ERR_WORDS: Dict[int, torch.Tensor] = {}
 
-# Tile shape the attention kernel consumes: 256 query rows (two tcgen05 M=128
-# tiles sharing every K/V tile) x 128 keys.  The mask builder accepts others
-# (multiples of 16 up to 256) for analysis.
-ATTN_BLOCK_Q = 256
+# Tile shape the attention kernel consumes: 128 query rows x 128 keys (one
+# tcgen05 M=128 tile per CTA, S and P double-buffered in TMEM).  The mask
+# builder accepts other shapes (multiples of 16 up to 256) for analysis.
+ATTN_BLOCK_Q = 128
 ATTN_BLOCK_K = 128
 
 

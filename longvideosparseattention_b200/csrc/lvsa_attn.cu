@@ -1,15 +1,26 @@
 // Block-sparse LVSA attention forward for sm_100a (tcgen05 + TMEM + TMA).
 //
-// One CTA per (128-row query tile, head, batch).  Warp roles:
-//   warps 0-3  softmax: thread r owns query row r (= TMEM lane r); reads S
-//              from TMEM, applies the in-tile frame mask on flagged tiles,
-//              online softmax in the log2 domain with lazy O rescaling,
-//              writes P (bf16/f16) to TMEM, final O / l epilogue.
-//   warp 4     TMA producer: Q once, then K and V tiles of the row's CSR
-//              list, read in place from the [B, N, H, D] tensors.
-//   warp 5     TMEM allocator + single-thread tcgen05.mma issuer:
-//              S_j = Q K_j^T (SS), then O += P_{j-1} V_{j-1} (TS, P from TMEM).
-// TMEM columns: S0 [0,128) S1 [128,256) O [256,256+D) P0 [384,448) P1 [448,512).
+// One CTA per (128-row query tile, head, batch); 320 threads:
+//   warps 0-7  softmax, two warps per query row: warp w owns key columns
+//              [64 (w / 4), +64) of rows 32 (w % 4) + lane (= TMEM lanes).
+//              The pair exchanges its partial row max through shared memory,
+//              then each warp applies the in-tile frame mask (flagged tiles
+//              only), exponentiates its 64 columns (log2 domain, lazy O
+//              rescale) and packs P to bf16/f16 into TMEM.
+//              Before the loop the same warps copy the query tile from global
+//              memory into TMEM (bf16 pairs, lane = row).
+//   warp 8     TMA producer: K and V tiles of the row's CSR list, read in
+//              place from the [B, N, H, D] tensors into a 3-stage (D=128) /
+//              6-stage (D=64) ring; K and V stages are released separately.
+//   warp 9     TMEM allocator + single-thread tcgen05.mma issuer:
+//              S(j+1) = Q K_{j+1}^T (A = Q from TMEM, B = K from shared memory,
+//              N = 128) is issued before O += P(j) V_j (A = P from TMEM), so the
+//              tensor pipe computes the next scores while the softmax works on
+//              the current ones.  With both A operands in TMEM the MMAs read only
+//              K and V from shared memory, which keeps its bandwidth for TMA.
+// TMEM columns: S0 [0,128) S1 [128,256) O [256,256+D) P [384,448)
+// Q [448, 448+D/2): S is double-buffered, so no MMA waits on the softmax of
+// the tile it is not consuming.
 //
 // Semantics follow lvsa_sdpa (lvsa/sparse_attention.py:643-706) with the
 // processor's text handling (lvsa/lvsa_processor.py:545-549, 584-591):
@@ -32,25 +43,22 @@
 namespace lvsa {
 namespace {
 
-constexpr int kBM = 128;           // rows of one tcgen05 M=128 tile
-constexpr int kQT = 2;             // query tiles per CTA
-constexpr int kBlockQ = kBM * kQT; // query rows per CTA (= CSR block_q)
+constexpr int kBM = 128;           // query rows per CTA (= CSR block_q)
+constexpr int kBlockQ = kBM;
 constexpr int kBN = 128;           // key tokens per tile (= CSR block_k)
 constexpr int kChunk = 128 * 128;  // one 128-row x 128-byte swizzle-128B slab
-constexpr int kSoftmaxWarps = 4 * kQT;
+constexpr int kSoftmaxWarps = 8;
 constexpr int kProducerWarp = kSoftmaxWarps;
 constexpr int kMmaWarp = kSoftmaxWarps + 1;
 constexpr int kThreads = 32 * (kSoftmaxWarps + 2);
 constexpr uint32_t kTmemCols = 512;
 constexpr float kNegInf = -INFINITY;
-#ifndef LVSA_EMU
-#define LVSA_EMU 0
-#endif
-// Exponentials per 8 evaluated by polynomial on the FMA pipe.
-constexpr int kEmuPer8 = LVSA_EMU;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O only when the max grows by > 2^8
 
 struct AttnParams {
+  const void* q;
+  const void* text_q;
+  int64_t q_sb, q_st, q_sh, tq_sb, tq_st, tq_sh;
   void* o;
   void* text_o;
   float* lse;
@@ -69,13 +77,13 @@ template <int D, int STAGES>
 struct Smem {
   static constexpr int kCh = D / 64;               // 128-byte column slabs per row
   static constexpr int kTile = kCh * kChunk;       // bytes of one 128 x D tile
-  static constexpr int kQ = 0;                     // kQT query tiles
-  static constexpr int kK = kQT * kTile;
+  static constexpr int kK = 0;
   static constexpr int kV = kK + STAGES * kTile;
   static constexpr int kBar = kV + STAGES * kTile;
-  static constexpr int kNumBars = 1 + 4 * STAGES + 3 * kQT + 1;
+  static constexpr int kNumBars = 1 + 4 * STAGES + 6 + 1;
   static constexpr int kMisc = kBar + kNumBars * 8;
-  static constexpr int kBytes = kMisc + 16 + 1024;  // + alignment slack
+  static constexpr int kRed = kMisc + 16;          // pair exchange: [2 parity][2 half][128 rows] f32 + i32
+  static constexpr int kBytes = kRed + 2 * 2 * 2 * kBM * 4 + 1024;  // + alignment slack
 };
 
 __device__ __forceinline__ uint32_t pack2(float a, float b, bool bf16) {
@@ -119,17 +127,13 @@ __device__ __forceinline__ void tile_mask(uint32_t (&am)[4], const AttnParams& p
   }
 }
 
-// S_q(j) = Q_q K_j^T as two N=64 halves (keys 0-63 -> columns 0-63, keys
-// 64-127 -> columns 64-127).  The high half overwrites P_q(j-1), so it is
-// issued separately once PV_q(j-1) has completed.
-template <int D, bool kBf16>
-__device__ __forceinline__ void issue_s_half(uint32_t dS, uint32_t q_base, uint32_t k_base, int half) {
-  constexpr uint32_t idS = idesc_f16(kBM, 64, kBf16, false);
-#pragma unroll
-  for (int kk = 0; kk < D / 16; ++kk) {
-    const uint32_t off = (kk >> 2) * kChunk + (kk & 3) * 32;
-    mma_ss(dS + half * 64, sdesc_sw128(q_base + off, 16, 1024),
-           sdesc_sw128(k_base + half * 64 * 128 + off, 16, 1024), idS, kk > 0);
+template <int N>
+__device__ __forceinline__ void tmem_st_q(uint32_t taddr, const uint32_t (&r)[N]) {
+  if constexpr (N == 32) {
+    tmem_st32(taddr, r);
+  } else {
+    static_assert(N == 16, "head_dim 64 or 128");
+    tmem_st16(taddr, r);
   }
 }
 
@@ -142,19 +146,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   using L = Smem<D, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem + L::kQ;
   uint8_t* sK = smem + L::kK;
   uint8_t* sV = smem + L::kV;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBar);
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;
   uint64_t* v_full = k_full + STAGES;
-  uint64_t* k_empty = v_full + STAGES;   // K stage free: every S of its tile done
-  uint64_t* v_empty = k_empty + STAGES;  // V stage free: every PV of its tile done
-  uint64_t* s_full = v_empty + STAGES;   // [kQT]
-  uint64_t* p_full = s_full + kQT;       // [kQT]
-  uint64_t* pv_done = p_full + kQT;      // [kQT]
-  uint64_t* drain = pv_done + kQT;
+  uint64_t* k_empty = v_full + STAGES;   // K stage free: the S of its tile is done
+  uint64_t* v_empty = k_empty + STAGES;  // V stage free: the PV of its tile is done
+  uint64_t* s_full = v_empty + STAGES;   // [2] S buffer b holds S(j), j % 2 == b
+  uint64_t* p_full = s_full + 2;         // [2] P buffer b written (and S buffer b read)
+  uint64_t* pv_done = p_full + 2;        // [2] PV(j) done, j % 2 == b
+  uint64_t* drain = pv_done + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMisc);
   volatile int* abort = reinterpret_cast<volatile int*>(smem + L::kMisc + 4);
   volatile int* never = reinterpret_cast<volatile int*>(smem + L::kMisc + 8);  // stays 0: drain waits
@@ -164,20 +167,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int beg = prm.indptr[row];
   const int n = prm.indptr[row + 1] - beg;
   const bool text_row = row >= prm.nqv;
-  const int tok0 = (text_row ? row - prm.nqv : row) * kBlockQ;
+  const int tok0 = (text_row ? row - prm.nqv : row) * kBM;
   const int hk = h / (prm.heads / prm.kv_heads);
 
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
+    mbar_init(q_full, 2 * 128);  // the softmax threads' copies of Q into TMEM
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&v_full[s], 1);
       mbar_init(&k_empty[s], 1);
       mbar_init(&v_empty[s], 1);
     }
-    for (int i = 0; i < kQT; ++i) {
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 128);
+      mbar_init(&p_full[i], 2 * 128);
       mbar_init(&pv_done[i], 1);
     }
     mbar_init(drain, 1);
@@ -193,40 +196,27 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  // TMEM columns: S_q [128q, 128q+128) (P_q in its upper 64), O_q [256 + Dq, 256 + D(q+1)).
-  auto tS = [&](int q) { return tmem + 128u * q; };
-  auto tO = [&](int q) { return tmem + 256u + static_cast<uint32_t>(D) * q; };
+  const uint32_t tS = tmem, tO = tmem + 256, tP = tmem + 384, tQ = tmem + 448;
 
   if (warp == kProducerWarp) {
     // ---------------------------------------------------------- producer
     if (lane == 0 && n > 0) {
-      const CUtensorMap* mq = text_row ? &tm_tq : &tm_q;
-      tma_prefetch_desc(mq);
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
-      mbar_expect_tx(q_full, kQT * L::kTile);
-#pragma unroll
-      for (int q = 0; q < kQT; ++q)
-#pragma unroll
-        for (int c = 0; c < L::kCh; ++c)
-          tma_load_4d(sQ + q * L::kTile + c * kChunk, mq, q_full, c * 64, h, tok0 + q * kBM, b);
       int issued = 0;
       for (int j = 0; j < n; ++j) {
         const int s = j % STAGES;
-        if (j >= STAGES && !mbar_wait(&k_empty[s], ((j / STAGES) - 1) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT))
-          break;
         const int kt = prm.indices[beg + j];
         const bool tt = kt >= prm.nkv;
         const int ktok = (tt ? kt - prm.nkv : kt) * kBN;
         const CUtensorMap* mk = tt ? &tm_tk : &tm_k;
         const CUtensorMap* mv = tt ? &tm_tv : &tm_v;
+        if (j >= STAGES && !mbar_wait(&k_empty[s], ((j / STAGES) - 1) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT))
+          break;
         mbar_expect_tx(&k_full[s], L::kTile);
 #pragma unroll
         for (int c = 0; c < L::kCh; ++c)
           tma_load_4d(sK + s * L::kTile + c * kChunk, mk, &k_full[s], c * 64, hk, ktok, b);
-        // K and V stages are released separately: K as soon as both S MMAs
-        // of its tile are done, V after both PVs, so the next K is in flight
-        // a full PV phase earlier.
         if (j >= STAGES && !mbar_wait(&v_empty[s], ((j / STAGES) - 1) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT))
           break;
         mbar_expect_tx(&v_full[s], L::kTile);
@@ -237,7 +227,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (*abort) {
         // Drain our own copies still in flight before the CTA retires.
-        mbar_wait(q_full, 0, never, nullptr, 0);
         for (int j = max(0, issued - STAGES); j < issued; ++j) {
           const int s = j % STAGES;
           mbar_wait(&k_full[s], (j / STAGES) & 1, never, nullptr, 0);
@@ -247,51 +236,47 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == kMmaWarp) {
     // ---------------------------------------------------------- MMA issuer
-    // Per key tile j:  PV_0(j), S_0lo(j+1), [PV_0(j) done] S_0hi(j+1),
-    //                  PV_1(j), S_1lo(j+1), [PV_1(j) done] S_1hi(j+1).
-    // While softmax q works on S_q(j+1) the tensor pipe runs the other tile's
-    // PV and S (1024 of the 2048 MMA cycles per key tile).
+    // Iteration j: S(j+1) into S buffer (j+1)%2 (free once the softmax has
+    // consumed S(j-1), i.e. P(j-1) arrived, which iteration j-1 waited for),
+    // then PV(j) once P(j) is in TMEM.
     if (lane == 0 && n > 0) {
+      constexpr uint32_t idS = idesc_f16(kBM, kBN, kBf16, false);
       constexpr uint32_t idO = idesc_f16(kBM, D, kBf16, true);
-      const uint32_t q_base = smem_u32(sQ), k_base = smem_u32(sK), v_base = smem_u32(sV);
+      const uint32_t k_base = smem_u32(sK), v_base = smem_u32(sV);
+      auto issue_s = [&](int jj) {
+        const uint32_t kb = k_base + (jj % STAGES) * L::kTile, dS = tS + (jj & 1) * 128;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * kChunk + (kk & 3) * 32;
+          mma_ts(dS, tQ + kk * 8, sdesc_sw128(kb + off, 16, 1024), idS, kk > 0);
+        }
+        mma_commit(&s_full[jj & 1]);
+        mma_commit(&k_empty[jj % STAGES]);
+      };
       bool ok = mbar_wait(q_full, 0, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT) &&
                 mbar_wait(&k_full[0], 0, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT);
       if (ok) {
         tc_fence_after();
-#pragma unroll
-        for (int q = 0; q < kQT; ++q) {
-          issue_s_half<D, kBf16>(tS(q), q_base + q * L::kTile, k_base, 0);
-          issue_s_half<D, kBf16>(tS(q), q_base + q * L::kTile, k_base, 1);
-          mma_commit(&s_full[q]);
-        }
-        mma_commit(&k_empty[0]);
+        issue_s(0);
       }
       for (int j = 0; ok && j < n; ++j) {
-        const int st = j % STAGES, st1 = (j + 1) % STAGES;
-        const bool has_next = j + 1 < n;
-        if (!mbar_wait(&v_full[st], (j / STAGES) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT)) break;
-        if (has_next && !mbar_wait(&k_full[st1], ((j + 1) / STAGES) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT))
-          break;
-        const uint32_t vb = v_base + st * L::kTile, kb1 = k_base + st1 * L::kTile;
-#pragma unroll
-        for (int q = 0; q < kQT; ++q) {
-          if (!(ok = mbar_wait(&p_full[q], j & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT))) break;
+        if (j + 1 < n) {
+          // S buffer (j+1)%2 last held S(j-1): P(j-1) arrived before PV(j-1) was issued.
+          if (!(ok = mbar_wait(&k_full[(j + 1) % STAGES], ((j + 1) / STAGES) & 1, abort, prm.err,
+                               LVSA_ERR_DEVICE_TIMEOUT)))
+            break;
           tc_fence_after();
-          const uint32_t tP = tS(q) + 64;
-#pragma unroll
-          for (int kk = 0; kk < kBN / 16; ++kk)
-            mma_ts(tO(q), tP + kk * 8, sdesc_sw128(vb + kk * 2048, kChunk, 1024), idO, (j > 0 || kk > 0));
-          mma_commit(&pv_done[q]);
-          if (q == kQT - 1) mma_commit(&v_empty[st]);
-          if (has_next) {
-            issue_s_half<D, kBf16>(tS(q), q_base + q * L::kTile, kb1, 0);
-            if (!(ok = mbar_wait(&pv_done[q], j & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT))) break;
-            tc_fence_after();
-            issue_s_half<D, kBf16>(tS(q), q_base + q * L::kTile, kb1, 1);
-            mma_commit(&s_full[q]);
-            if (q == kQT - 1) mma_commit(&k_empty[st1]);
-          }
+          issue_s(j + 1);
         }
+        if (!(ok = mbar_wait(&p_full[j & 1], (j >> 1) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT))) break;
+        if (!(ok = mbar_wait(&v_full[j % STAGES], (j / STAGES) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT))) break;
+        tc_fence_after();
+        const uint32_t vb = v_base + (j % STAGES) * L::kTile, pa = tP;
+#pragma unroll
+        for (int kk = 0; kk < kBN / 16; ++kk)
+          mma_ts(tO, pa + kk * 8, sdesc_sw128(vb + kk * 2048, kChunk, 1024), idO, (j > 0 || kk > 0));
+        mma_commit(&pv_done[j & 1]);
+        mma_commit(&v_empty[j % STAGES]);
       }
       // Make sure every MMA this thread issued has retired before TMEM is freed.
       mma_commit(drain);
@@ -299,114 +284,142 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ---------------------------------------------------------- softmax
-    const int q = warp >> 2;                     // query tile of this warpgroup
-    const int r = threadIdx.x & (kBM - 1);       // row in the tile = TMEM lane
+    const int half = warp >> 2;                  // key columns [64 half, 64 half + 64)
+    const int r = ((warp & 3) << 5) | lane;      // query row = TMEM lane
+    const uint32_t pair_bar = 1 + (warp & 3);    // named barrier shared with the partner warp
+    float* red_max = reinterpret_cast<float*>(smem + L::kRed);           // [2][2][128]
+    int* red_ok = reinterpret_cast<int*>(smem + L::kRed + 2 * 2 * kBM * 4);
+    // Exchange one value with the partner warp (same rows, other 64 columns).
+    // Both warps see the same (mine, theirs) flags and take the same branch.
+    auto xchg = [&](int par, float v, bool mine, float& other) -> bool {
+      red_max[(par * 2 + half) * kBM + r] = v;
+      red_ok[(par * 2 + half) * kBM + r] = mine ? 1 : 0;
+      asm volatile("bar.sync %0, 64;" ::"r"(pair_bar) : "memory");
+      other = red_max[(par * 2 + (half ^ 1)) * kBM + r];
+      const bool theirs = red_ok[(par * 2 + (half ^ 1)) * kBM + r] != 0;
+      return __all_sync(0xFFFFFFFFu, mine && theirs);
+    };
     const int seg_len = text_row ? prm.n_text : prm.n_video;
-    const int tok = tok0 + q * kBM + r;
+    const int tok = tok0 + r;
     const bool valid = tok < seg_len;
     const int fq = text_row ? 0 : min(tok / prm.P, prm.T - 1);
     const uint32_t* fbits = prm.frame_bits + static_cast<size_t>(fq) * prm.words;
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    const uint32_t tSq = tS(q) + lane_base, tPq = tSq + 64, tOq = tO(q) + lane_base;
+    const uint32_t tSr = tS + lane_base + half * 64;      // my 64 S columns (buffer 0)
+    const uint32_t tPr = tP + lane_base + half * 32;      // my 32 packed P columns
+    const uint32_t tOr = tO + lane_base + half * (D / 2);  // my D/2 O columns
     const float sl2 = prm.scale_log2;
+    if (n > 0) {
+      // Query row -> TMEM: my D/2 elements as D/4 packed words at Q columns
+      // [448 + half D/4, +D/4); rows past the segment are zero.
+      const uint16_t* qsrc = nullptr;
+      if (valid) {
+        qsrc = text_row ? reinterpret_cast<const uint16_t*>(prm.text_q) + b * prm.tq_sb +
+                              static_cast<int64_t>(tok) * prm.tq_st + h * prm.tq_sh
+                        : reinterpret_cast<const uint16_t*>(prm.q) + b * prm.q_sb +
+                              static_cast<int64_t>(tok) * prm.q_st + h * prm.q_sh;
+        qsrc += half * (D / 2);
+      }
+      uint32_t qw[D / 4];
+#pragma unroll
+      for (int i = 0; i < D / 16; ++i) {  // D/2 bf16 = D/16 16-byte words
+        const uint4 v4 = qsrc ? reinterpret_cast<const uint4*>(qsrc)[i] : make_uint4(0u, 0u, 0u, 0u);
+        qw[4 * i] = v4.x; qw[4 * i + 1] = v4.y; qw[4 * i + 2] = v4.z; qw[4 * i + 3] = v4.w;
+      }
+      tmem_st_q<D / 4>(tQ + lane_base + half * (D / 4), qw);
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(q_full);
+    }
     float m = kNegInf, l = 0.f;
-    bool ok = true;
+    bool ok = true, fail = false;  // fail: a wait below timed out; reported at the next exchange
     int flag_next = n > 0 ? prm.flags[beg] : 0;
     int kt_next = n > 0 ? prm.indices[beg] : 0;
     for (int j = 0; j < n; ++j) {
-      const int flag = flag_next, kt = kt_next;
+      const int flag = flag_next, kt = kt_next, bb = j & 1;
       if (j + 1 < n) {
         flag_next = prm.flags[beg + j + 1];
         kt_next = prm.indices[beg + j + 1];
       }
-      ok = __all_sync(0xFFFFFFFFu, mbar_wait(&s_full[q], j & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT));
-      if (!ok) break;
-      tc_fence_after();
-      // Both 64-column halves of the S row are loaded under one wait; P
-      // (keys 0-63 -> columns 64-95, keys 64-127 -> 96-127) then only
-      // overwrites S columns already held in registers.
-      uint32_t am[4] = {~0u, ~0u, ~0u, ~0u};
-      if (flag) tile_mask(am, prm, kt, text_row, fbits);
-      uint32_t lo[64], hi[64];
-      tmem_ld64x2(tSq, tSq + 64, lo, hi);
-      if (flag) {
+      const bool got =
+          __all_sync(0xFFFFFFFFu, mbar_wait(&s_full[bb], (j >> 1) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT));
+      uint32_t sv[64];
+      float pm = kNegInf;
+      if (got) {
+        tc_fence_after();
+        tmem_ld64(tSr + bb * 128, sv);
+        if (flag) {
+          uint32_t am[4];
+          tile_mask(am, prm, kt, text_row, fbits);
 #pragma unroll
-        for (int i = 0; i < 64; ++i) {
-          if (!((am[i >> 5] >> (i & 31)) & 1u)) lo[i] = __float_as_uint(kNegInf);
-          if (!((am[2 + (i >> 5)] >> (i & 31)) & 1u)) hi[i] = __float_as_uint(kNegInf);
+          for (int i = 0; i < 64; ++i)
+            if (!((am[2 * half + (i >> 5)] >> (i & 31)) & 1u)) sv[i] = __float_as_uint(kNegInf);
         }
+        float mx8[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) mx8[i] = __uint_as_float(sv[i]);
+#pragma unroll
+        for (int i = 8; i < 64; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], __uint_as_float(sv[i]));
+#pragma unroll
+        for (int w = 4; w >= 1; w >>= 1)
+#pragma unroll
+          for (int i = 0; i < w; ++i) mx8[i] = fmaxf(mx8[i], mx8[i + w]);
+        pm = mx8[0];
       }
-      // 16 independent max chains (dependency depth 8 instead of 16).
-      float mx16[16];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        mx16[i] = __uint_as_float(lo[i]);
-        mx16[8 + i] = __uint_as_float(hi[i]);
-      }
-#pragma unroll
-      for (int i = 8; i < 64; ++i) {
-        mx16[i & 7] = fmaxf(mx16[i & 7], __uint_as_float(lo[i]));
-        mx16[8 + (i & 7)] = fmaxf(mx16[8 + (i & 7)], __uint_as_float(hi[i]));
-      }
-#pragma unroll
-      for (int w = 8; w >= 1; w >>= 1)
-#pragma unroll
-        for (int i = 0; i < w; ++i) mx16[i] = fmaxf(mx16[i], mx16[i + w]);
-      const float mx = mx16[0];
-      const float m_new = fmaxf(m, mx * sl2);
+      float other;
+      ok = xchg(bb, pm, got && !fail, other);
+      if (!ok) break;
+      const float m_new = fmaxf(m, fmaxf(pm, other) * sl2);
       if (j == 0) {
         m = m_new;
       } else {
-        // Lazy rescale: O_q is quiescent here (PV_q(j-1) completed before S_q(j) was issued).
+        // Lazy rescale of my half of O (both warps of the pair decide alike).
         const bool need = m_new > m + kRescaleThreshold;
         if (__any_sync(0xFFFFFFFFu, need)) {
+          // O must hold PV(j-1) completely before it is scaled.
+          fail |= !__all_sync(0xFFFFFFFFu, mbar_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, abort,
+                                                     prm.err, LVSA_ERR_DEVICE_TIMEOUT));
+          tc_fence_after();
           const float alpha = need ? ex2_approx(m - m_new) : 1.f;
           if (need) m = m_new;
 #pragma unroll
-          for (int c = 0; c < D / 32; ++c) {
+          for (int c = 0; c < D / 64; ++c) {
             uint32_t t[32];
-            tmem_ld32(tOq + c * 32, t);
+            tmem_ld32(tOr + c * 32, t);
 #pragma unroll
             for (int i = 0; i < 32; ++i) t[i] = __float_as_uint(__uint_as_float(t[i]) * alpha);
-            tmem_st32(tOq + c * 32, t);
+            tmem_st32(tOr + c * 32, t);
           }
           l *= alpha;
         }
       }
       const float mu = (m == kNegInf) ? 0.f : m;
-      // Packed fp32x2: argument (s*scale - m) and the row sum run two lanes
-      // per instruction; kEmuPer8 of every 8 exponentials use ex2_poly2 on
-      // the FMA pipe, the rest MUFU.
       const uint64_t sl2x2 = f2_pack(sl2, sl2), nmu2 = f2_pack(-mu, -mu);
       uint64_t acc2[4] = {0ull, 0ull, 0ull, 0ull};
+      uint32_t pk[32];
 #pragma unroll
-      for (int hc = 0; hc < 2; ++hc) {
-        const uint32_t* sv = hc ? hi : lo;
-        uint32_t pk[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int e = 2 * i;
-          const uint64_t x2 = f2_fma(f2_pack(__uint_as_float(sv[e]), __uint_as_float(sv[e + 1])), sl2x2, nmu2);
-          float xa, xc, a, c;
-          f2_unpack(x2, xa, xc);
-          if ((e & 7) < kEmuPer8) {
-            ex2_poly2(xa, xc, a, c);
-          } else {
-            a = ex2_approx(xa);
-            c = ex2_approx(xc);
-          }
-          acc2[i & 3] = f2_add(acc2[i & 3], f2_pack(a, c));
-          pk[i] = pack2(a, c, kBf16);
-        }
-        tmem_st32(tPq + hc * 32, pk);
+      for (int i = 0; i < 32; ++i) {
+        const uint64_t x2 = f2_fma(f2_pack(__uint_as_float(sv[2 * i]), __uint_as_float(sv[2 * i + 1])), sl2x2, nmu2);
+        float xa, xc;
+        f2_unpack(x2, xa, xc);
+        const float a = ex2_approx(xa), c = ex2_approx(xc);
+        acc2[i & 3] = f2_add(acc2[i & 3], f2_pack(a, c));
+        pk[i] = pack2(a, c, kBf16);
       }
+      // The single P buffer last fed PV(j-1).
+      if (j >= 1) {
+        fail |= !__all_sync(0xFFFFFFFFu, mbar_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, abort, prm.err,
+                                                   LVSA_ERR_DEVICE_TIMEOUT));
+        tc_fence_after();
+      }
+      tmem_st32(tPr, pk);
       float acc[8];
 #pragma unroll
       for (int i = 0; i < 4; ++i) f2_unpack(acc2[i], acc[2 * i], acc[2 * i + 1]);
       l += ((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7]));
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&p_full[q]);
+      mbar_arrive(&p_full[bb]);
     }
     // ---------------------------------------------------------- epilogue
     using Elem = typename std::conditional<kBf16, __nv_bfloat16, __half>::type;
@@ -421,15 +434,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       obase = reinterpret_cast<Elem*>(prm.o) + b * prm.o_sb + static_cast<int64_t>(tok) * prm.o_st + h * prm.o_sh;
       if (prm.lse) lse = prm.lse + (static_cast<int64_t>(b) * prm.heads + h) * prm.n_video + tok;
     }
+    if (obase) obase += half * (D / 2);
     if (ok && n > 0) {
-      ok = __all_sync(0xFFFFFFFFu, mbar_wait(&pv_done[q], (n - 1) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT));
-      if (ok) {
+      const bool got = __all_sync(0xFFFFFFFFu, mbar_wait(&pv_done[(n - 1) & 1], ((n - 1) >> 1) & 1, abort,
+                                                        prm.err, LVSA_ERR_DEVICE_TIMEOUT));
+      float l_other;
+      if (xchg(n & 1, l, got && !fail, l_other)) {
+        const float lt = l + l_other;
         tc_fence_after();
-        const float inv = (l > 0.f) ? 1.f / l : 0.f;
+        const float inv = (lt > 0.f) ? 1.f / lt : 0.f;
 #pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
+        for (int c = 0; c < D / 64; ++c) {
           uint32_t t[32];
-          tmem_ld32(tOq + c * 32, t);
+          tmem_ld32(tOr + c * 32, t);
           if (valid && obase) {
             uint32_t pk[16];
 #pragma unroll
@@ -440,15 +457,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int i = 0; i < 4; ++i) dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
           }
         }
-        if (valid && lse) *lse = (l > 0.f) ? (m + __log2f(l)) * 0.69314718055994531f : kNegInf;
+        if (valid && lse && half == 0) *lse = (lt > 0.f) ? (m + __log2f(lt)) * 0.69314718055994531f : kNegInf;
       }
     } else if (n == 0 && valid) {
       if (obase) {
         uint4* dst = reinterpret_cast<uint4*>(obase);
 #pragma unroll
-        for (int i = 0; i < D / 8; ++i) dst[i] = make_uint4(0u, 0u, 0u, 0u);
+        for (int i = 0; i < D / 16; ++i) dst[i] = make_uint4(0u, 0u, 0u, 0u);
       }
-      if (lse) *lse = kNegInf;
+      if (lse && half == 0) *lse = kNegInf;
     }
   }
 
@@ -523,6 +540,10 @@ int launch(const LvsaAttnArgs* a, cudaStream_t stream) {
     mtq = mq;
   }
   AttnParams p;
+  p.q = a->q.ptr;
+  p.text_q = text_rows ? a->text_q.ptr : nullptr;
+  p.q_sb = a->q.stride_b; p.q_st = a->q.stride_t; p.q_sh = a->q.stride_h;
+  p.tq_sb = a->text_q.stride_b; p.tq_st = a->text_q.stride_t; p.tq_sh = a->text_q.stride_h;
   p.o = a->o.ptr;
   p.text_o = text_rows ? a->text_o.ptr : nullptr;
   p.lse = a->lse;
@@ -571,8 +592,8 @@ extern "C" int lvsa_attn_fwd(const LvsaAttnArgs* a, void* stream) {
   const bool bf16 = a->dtype == LVSA_DTYPE_BF16;
   if (a->dtype != LVSA_DTYPE_BF16 && a->dtype != LVSA_DTYPE_F16) return LVSA_ERR_UNSUPPORTED;
   switch (a->head_dim) {
-    case 128: return bf16 ? launch<128, 2, true>(a, s) : launch<128, 2, false>(a, s);
-    case 64: return bf16 ? launch<64, 5, true>(a, s) : launch<64, 5, false>(a, s);
+    case 128: return bf16 ? launch<128, 3, true>(a, s) : launch<128, 3, false>(a, s);
+    case 64: return bf16 ? launch<64, 6, true>(a, s) : launch<64, 6, false>(a, s);
     default: return LVSA_ERR_UNSUPPORTED;
   }
 }
