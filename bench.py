@@ -42,6 +42,9 @@ CONFIGS = {
 }
 METRIC = "sparse-attn ms/layer & useful TFLOPS (% of B200 peak) at 1/2/4/8 GPUs"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+# DRAM bytes (read + write) per attention launch, from one ncu capture of a
+# full-size layer (profiles/lvsa_attn_cfg2_full.md); null where not captured.
+NCU_TRAFFIC_BYTES = {"cfg2": 1.585e9}
 
 
 def log(*a):
@@ -247,7 +250,9 @@ def run_b200(args, cfg):
                        "l2": "30 distinct layer inputs (35 GB) cycled: inputs exceed L2, no flush",
                        "parallelism": f"replicas x{world} (independent layers per rank)"},
             "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak,
-                         "unit": "TFLOP/s", "frac": round(achieved / peak, 4), "traffic": None,
+                         "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
+                         "traffic": NCU_TRAFFIC_BYTES.get(args.config),
+                         "algorithmic_bytes": 4 * T * P * H * D * 2 + 4 * nt * H * D * 2,
                          "peak_source": f"{pk_kind} bf16_tflops_sustained (kernel runs back-to-back in a long step)",
                          "mean_launch_ms": round(mean_launch, 4)},
             "clocks": clk.summary(),
