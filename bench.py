@@ -180,7 +180,24 @@ def run_b200(args, cfg):
     L = cfg["layers"]
     T, P, H, D, nt = cfg["T"], cfg["P"], cfg["H"], cfg["D"], cfg["n_text"]
     flop_tiles, flop_exact = flops_for(cfg)
-    layers = [seeded_layer(cfg, rank * L + i, dev) for i in range(L)]
+    ulysses = args.parallel == "ulysses" and world > 1
+    if ulysses:
+        # Strong scaling: the same 30 layers on every N; each rank holds its
+        # contiguous token shard of q/k/v (heads are scattered by all-to-all).
+        from longvideosparseattention_b200.ulysses import shard_sizes, ulysses_attention
+        if H % world:
+            raise SystemExit(f"Ulysses needs heads ({H}) divisible by the GPU count ({world})")
+        sizes = shard_sizes(T * P, world)
+        a0 = sum(sizes[:rank])
+        layers = []
+        for i in range(L):
+            lay = seeded_layer(cfg, i, dev)
+            lay[:3] = [x[:, a0:a0 + sizes[rank]].contiguous() for x in lay[:3]]
+            layers.append(lay)
+            del lay
+        torch.cuda.empty_cache()
+    else:
+        layers = [seeded_layer(cfg, rank * L + i, dev) for i in range(L)]
     outs = [torch.empty_like(layers[0][0]) for _ in range(2)]
     touts = [torch.empty_like(layers[0][3]) for _ in range(2)] if nt else [None, None]
     stream = torch.cuda.current_stream(dev)
@@ -195,7 +212,11 @@ def run_b200(args, cfg):
             if ev is not None:
                 ev[i][0].record(stream)
             tx = (lay[3], lay[4], lay[5]) if nt else (None, None, None)
-            block_sparse_attention(lay[0], lay[1], lay[2], mask, *tx, out=outs[i & 1], text_out=touts[i & 1])
+            if ulysses:
+                ulysses_attention(lay[0], lay[1], lay[2], sizes,
+                                  lambda q, k, v, a, b_, c: block_sparse_attention(q, k, v, mask, a, b_, c), *tx)
+            else:
+                block_sparse_attention(lay[0], lay[1], lay[2], mask, *tx, out=outs[i & 1], text_out=touts[i & 1])
             if ev is not None:
                 ev[i][1].record(stream)
 
@@ -226,29 +247,32 @@ def run_b200(args, cfg):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_max = float(t.item())
     ms_step = ms_max / args.steps
-    total_flop = flop_tiles * L * args.steps * world
+    total_flop = flop_tiles * L * args.steps * (1 if ulysses else world)
     value = total_flop / (ms_max * 1e-3) / 1e12
 
     # ---- e2e through the public API with pinned host buffers (copies inside the timed region)
     e2e = None
-    if not args.no_e2e:
+    if not args.no_e2e and not ulysses:
         e2e = run_e2e(args, cfg, dev, world, flop_tiles)
 
     if rank == 0:
         pk, pk_kind = peaks()
         mean_launch = statistics.mean(kern_ms)
-        achieved = flop_tiles / (mean_launch * 1e-3) / 1e12
+        # per timed layer call: H/world heads under Ulysses (all-to-all included)
+        achieved = flop_tiles / (world if ulysses else 1) / (mean_launch * 1e-3) / 1e12
         peak = pk.get("bf16_tflops_sustained", pk.get("bf16_tflops"))
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 3),
-            "ms_per_layer": round(ms_step / L, 4), "higher_is_better": True, "scaling": "weak",
+            "ms_per_layer": round(ms_step / L, 4), "higher_is_better": True,
+            "scaling": "strong" if ulysses else "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1)/sqrt(D), RoPE-3D)",
             "config": {"workload": args.config, "desc": cfg["desc"], "layers_per_step": L,
                        "tokens": T * P + nt, "heads": H, "head_dim": D, "tile": "128x128",
                        "flop_tiles_per_layer": flop_tiles, "flop_exact_per_layer": flop_exact,
                        "l2": "30 distinct layer inputs (35 GB) cycled: inputs exceed L2, no flush",
-                       "parallelism": f"replicas x{world} (independent layers per rank)"},
+                       "parallelism": (f"ulysses x{world} (heads scattered by NCCL all-to-all)" if ulysses
+                                       else f"replicas x{world} (independent layers per rank)")},
             "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak,
                          "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
                          "traffic": NCU_TRAFFIC_BYTES.get(args.config),
@@ -391,6 +415,9 @@ def main():
     ap.add_argument("--config", default="cfg2", choices=sorted(CONFIGS))
     ap.add_argument("--layers", type=int, default=None, help="override layers per step")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--parallel", default="replicas", choices=["replicas", "ulysses"],
+                    help="N>1: independent layers per rank (weak scaling) or Ulysses head "
+                         "parallelism over one set of layers (strong scaling)")
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     args = ap.parse_args()
