@@ -216,7 +216,8 @@ def run_b200(args, cfg):
                 ulysses_attention(lay[0], lay[1], lay[2], sizes,
                                   lambda q, k, v, a, b_, c: block_sparse_attention(q, k, v, mask, a, b_, c), *tx)
             else:
-                block_sparse_attention(lay[0], lay[1], lay[2], mask, *tx, out=outs[i & 1], text_out=touts[i & 1])
+                block_sparse_attention(lay[0], lay[1], lay[2], mask, *tx, out=outs[i & 1], text_out=touts[i & 1],
+                                       fp8=args.fp8)
             if ev is not None:
                 ev[i][1].record(stream)
 
@@ -266,7 +267,8 @@ def run_b200(args, cfg):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 3),
             "ms_per_layer": round(ms_step / L, 4), "higher_is_better": True,
             "scaling": "strong" if ulysses else "weak",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1)/sqrt(D), RoPE-3D)",
+            "vs_baseline": None, "dtype": "e4m3 (QK, PV; fp32 accumulate)" if args.fp8 else "bf16",
+            "data": "synthetic (seeded N(0,1)/sqrt(D), RoPE-3D)",
             "config": {"workload": args.config, "desc": cfg["desc"], "layers_per_step": L,
                        "tokens": T * P + nt, "heads": H, "head_dim": D, "tile": "128x128",
                        "flop_tiles_per_layer": flop_tiles, "flop_exact_per_layer": flop_exact,
@@ -280,7 +282,7 @@ def run_b200(args, cfg):
                          "peak_source": f"{pk_kind} bf16_tflops_sustained (kernel runs back-to-back in a long step)",
                          "mean_launch_ms": round(mean_launch, 4)},
             "clocks": clk.summary(),
-            "gpu_launches": (4 + L) * args.steps,
+            "gpu_launches": (4 + L * (7 if args.fp8 else 1)) * args.steps,
             "e2e": e2e,
         }
         if args.cpu_baseline:
@@ -415,6 +417,8 @@ def main():
     ap.add_argument("--config", default="cfg2", choices=sorted(CONFIGS))
     ap.add_argument("--layers", type=int, default=None, help="override layers per step")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--fp8", action="store_true",
+                    help="E4M3 QK/PV with per-tile scales (quantisation inside the timed step)")
     ap.add_argument("--parallel", default="replicas", choices=["replicas", "ulysses"],
                     help="N>1: independent layers per rank (weak scaling) or Ulysses head "
                          "parallelism over one set of layers (strong scaling)")

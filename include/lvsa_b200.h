@@ -128,6 +128,38 @@ typedef struct LvsaAttnArgs {
  * frame's attended set plus all text, text rows attend everything. */
 int lvsa_attn_fwd(const LvsaAttnArgs* args, void* stream);
 
+/* ---------------------------------------------------------------- FP8 mode
+ * E4M3 QK / PV with per-tile scales (no counterpart in the reference, which
+ * has no FP8 path; BASELINE cfg3 asks for this variant).
+ *   Q, K: one scale per (batch, head, 128-token tile) = amax / 448.
+ *   V:    one scale per (batch, head, 128-token tile) plus a per-(batch, head)
+ *         reference (the max tile scale); the kernel folds scale_j / reference
+ *         into P before rounding it to E4M3, and multiplies O by the reference.
+ */
+enum { LVSA_DTYPE_E4M3 = 2 };
+
+/* Quantise one [B, N, heads, D] bf16/f16 tensor to a contiguous
+ * [B, N, heads, D] E4M3 copy `out8` with scales [B, heads, ceil(N/128)].
+ * `head_max` (optional, [B, heads] fp32) receives atomicMax of the tile scales
+ * and must hold zeros (or a smaller running max) before the call. */
+int lvsa_quantize_e4m3(const LvsaTensor* in, int32_t dtype, int32_t batch, int32_t n, int32_t heads,
+                       int32_t head_dim, void* out8, float* scales, float* head_max, void* stream);
+
+typedef struct LvsaFp8Scales {
+  const float* q;       /* [B, heads, ceil(n_video/128)]       */
+  const float* k;       /* [B, kv_heads, ceil(n_video/128)]    */
+  const float* v;       /* [B, kv_heads, ceil(n_video/128)]    */
+  const float* text_q;  /* [B, heads, ceil(n_text/128)] or NULL  */
+  const float* text_k;
+  const float* text_v;
+  const float* v_ref;   /* [B, kv_heads]: max V tile scale over video + text */
+} LvsaFp8Scales;
+
+/* FP8 attention: `args` as for lvsa_attn_fwd with q/k/v/text_* pointing at the
+ * E4M3 copies (contiguous [B, N, H, D] bytes; strides in elements = bytes) and
+ * `dtype` naming the OUTPUT type (bf16 or f16).  head_dim 128 only. */
+int lvsa_attn_fwd_fp8(const LvsaAttnArgs* args, const LvsaFp8Scales* scales, void* stream);
+
 /* Human-readable name of a status code. */
 const char* lvsa_status_str(int status);
 

@@ -26,8 +26,9 @@ LVSA_DTYPE_BF16 = 0
 LVSA_DTYPE_F16 = 1
 LVSA_MAX_FRAMES = 2048
 
-EXPORTED_SYMBOLS = ("lvsa_mask_layout", "lvsa_build_mask", "lvsa_attn_fwd", "lvsa_status_str",
-                    "lvsa_abi_version")
+EXPORTED_SYMBOLS = ("lvsa_mask_layout", "lvsa_build_mask", "lvsa_attn_fwd", "lvsa_quantize_e4m3",
+                    "lvsa_attn_fwd_fp8", "lvsa_status_str", "lvsa_abi_version")
+LVSA_DTYPE_E4M3 = 2
 
 _i32, _i64, _vp = ctypes.c_int32, ctypes.c_int64, ctypes.c_void_p
 
@@ -68,6 +69,10 @@ class LvsaAttnArgs(ctypes.Structure):
                 ("tile_flags", _vp), ("error_word", _vp)]
 
 
+class LvsaFp8Scales(ctypes.Structure):
+    _fields_ = [(n, _vp) for n in ("q", "k", "v", "text_q", "text_k", "text_v", "v_ref")]
+
+
 _lib = None
 _lock = threading.Lock()
 
@@ -96,6 +101,11 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
         lib.lvsa_build_mask.restype = ctypes.c_int
         lib.lvsa_attn_fwd.argtypes = [ctypes.POINTER(LvsaAttnArgs), _vp]
         lib.lvsa_attn_fwd.restype = ctypes.c_int
+        lib.lvsa_quantize_e4m3.argtypes = [ctypes.POINTER(LvsaTensor), _i32, _i32, _i32, _i32, _i32, _vp, _vp,
+                                           _vp, _vp]
+        lib.lvsa_quantize_e4m3.restype = ctypes.c_int
+        lib.lvsa_attn_fwd_fp8.argtypes = [ctypes.POINTER(LvsaAttnArgs), ctypes.POINTER(LvsaFp8Scales), _vp]
+        lib.lvsa_attn_fwd_fp8.restype = ctypes.c_int
         lib.lvsa_status_str.argtypes = [ctypes.c_int]
         lib.lvsa_status_str.restype = ctypes.c_char_p
         lib.lvsa_abi_version.argtypes = []

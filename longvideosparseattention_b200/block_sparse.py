@@ -193,13 +193,33 @@ def _prep(x: Optional[torch.Tensor], dtype: torch.dtype) -> Optional[torch.Tenso
     return x
 
 
+def quantize_e4m3(x: torch.Tensor, head_max: Optional[torch.Tensor] = None):
+    """[B, N, H, D] bf16/fp16 -> (contiguous E4M3 bytes [B, N, H, D] uint8,
+    per-128-token-tile scales [B, H, ceil(N/128)] fp32).  ``head_max`` [B, H]
+    fp32 receives the running max of the tile scales."""
+    B, Nn, H, D = x.shape
+    if x.dtype not in _DTYPES:
+        x = x.to(torch.bfloat16)
+    if x.stride(-1) != 1:
+        x = x.contiguous()
+    q8 = torch.empty(B, Nn, H, D, dtype=torch.uint8, device=x.device)
+    sc = torch.empty(B, H, -(-Nn // 128), dtype=torch.float32, device=x.device)
+    with torch.cuda.device(x.device):
+        st = N.load().lvsa_quantize_e4m3(ctypes.byref(_tview(x)), _DTYPES[x.dtype], B, Nn, H, D,
+                                         q8.data_ptr(), sc.data_ptr(),
+                                         head_max.data_ptr() if head_max is not None else None,
+                                         _stream_ptr(x.device))
+    N.check(st, "lvsa_quantize_e4m3")
+    return q8, sc
+
+
 def block_sparse_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, mask: BlockMask,
                            text_q: Optional[torch.Tensor] = None,
                            text_k: Optional[torch.Tensor] = None,
                            text_v: Optional[torch.Tensor] = None,
                            scale: Optional[float] = None, return_lse: bool = False,
                            out: Optional[torch.Tensor] = None,
-                           text_out: Optional[torch.Tensor] = None):
+                           text_out: Optional[torch.Tensor] = None, fp8: bool = False):
     """LVSA attention of one layer on the GPU.
 
     q [B, Nv, H, D], k/v [B, Nv, Hkv, D] (video, frame-major tokens);
@@ -236,6 +256,21 @@ def block_sparse_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, ma
         lse = torch.empty(B, H, Nv, dtype=torch.float32, device=q.device)
         if tq is not None:
             tlse = torch.empty(B, H, Nt, dtype=torch.float32, device=q.device)
+    sc_c = None
+    if fp8:
+        # E4M3 copies with per-tile scales; V's tile scales share one per-head reference.
+        vref = torch.zeros(B, Hkv, dtype=torch.float32, device=q.device)
+        qc, qs = quantize_e4m3(qc)
+        kc, ks = quantize_e4m3(kc)
+        vc, vs = quantize_e4m3(vc, vref)
+        tqs = tks = tvs = None
+        if tk is not None:
+            tk, tks = quantize_e4m3(tk)
+            tv, tvs = quantize_e4m3(tv, vref)
+        if tq is not None:
+            tq, tqs = quantize_e4m3(tq)
+        keep = (qs, ks, vs, tqs, tks, tvs, vref)
+        sc_c = N.LvsaFp8Scales(*[t.data_ptr() if t is not None else None for t in keep])
     args = N.LvsaAttnArgs(
         _tview(qc), _tview(kc), _tview(vc), _tview(o), _tview(tq), _tview(tk), _tview(tv), _tview(to),
         lse.data_ptr() if lse is not None else None, tlse.data_ptr() if tlse is not None else None,
@@ -245,8 +280,11 @@ def block_sparse_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, ma
         mask.frame_bits.data_ptr(), mask.tile_indptr.data_ptr(), mask.tile_indices.data_ptr(),
         mask.tile_flags.data_ptr(), error_word(q.device).data_ptr())
     with torch.cuda.device(q.device):
-        st = N.load().lvsa_attn_fwd(ctypes.byref(args), _stream_ptr(q.device))
-    N.check(st, "lvsa_attn_fwd")
+        if fp8:
+            st = N.load().lvsa_attn_fwd_fp8(ctypes.byref(args), ctypes.byref(sc_c), _stream_ptr(q.device))
+        else:
+            st = N.load().lvsa_attn_fwd(ctypes.byref(args), _stream_ptr(q.device))
+    N.check(st, "lvsa_attn_fwd_fp8" if fp8 else "lvsa_attn_fwd")
     if cdt != in_dtype:
         o = o.to(in_dtype)
         to = to.to(in_dtype) if to is not None else None

@@ -29,6 +29,7 @@
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+#include <cuda_fp8.h>
 #include <cuda_runtime.h>
 
 #include <cmath>
@@ -71,11 +72,21 @@ struct AttnParams {
   const int32_t* indices;
   const uint8_t* flags;
   int* err;
+  // FP8 mode only: per-tile scales [B, H(kv), tiles] and the per-head V reference.
+  const float* qs;
+  const float* ks;
+  const float* vs;
+  const float* tqs;
+  const float* tks;
+  const float* tvs;
+  const float* vref;
+  int nqt_all, nkt;  // query / key tiles of the text segment
 };
 
-template <int D, int STAGES>
+template <int D, int STAGES, bool kFp8 = false>
 struct Smem {
-  static constexpr int kCh = D / 64;               // 128-byte column slabs per row
+  static constexpr int kElem = kFp8 ? 1 : 2;       // bytes per element
+  static constexpr int kCh = D * kElem / 128;      // 128-byte column slabs per row
   static constexpr int kTile = kCh * kChunk;       // bytes of one 128 x D tile
   static constexpr int kK = 0;
   static constexpr int kV = kK + STAGES * kTile;
@@ -137,13 +148,37 @@ __device__ __forceinline__ void tmem_st_q(uint32_t taddr, const uint32_t (&r)[N]
   }
 }
 
-template <int D, int STAGES, bool kBf16>
+// tcgen05.mma kind::f8f6f4 (E4M3 x E4M3 -> fp32), A from TMEM.
+__device__ __forceinline__ void mma_ts_f8(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+template <bool kFp8>
+__device__ __forceinline__ void mma_ts_any(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t idesc, uint32_t acc) {
+  if constexpr (kFp8) mma_ts_f8(d, a_tmem, b, idesc, acc);
+  else mma_ts(d, a_tmem, b, idesc, acc);
+}
+
+__device__ __forceinline__ uint32_t pack4_e4m3(float a, float b, float c, float d) {
+  const __nv_fp8x2_storage_t lo = __nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3);
+  const __nv_fp8x2_storage_t hi = __nv_cvt_float2_to_fp8x2(make_float2(c, d), __NV_SATFINITE, __NV_E4M3);
+  return static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+}
+
+// kBf16: type of O (and of Q/K/V unless kFp8).  kFp8: Q/K/V are E4M3 copies
+// with per-tile scales (QK^T and PV on kind::f8f6f4, P rounded to E4M3).
+template <int D, int STAGES, bool kBf16, bool kFp8 = false>
 __global__ void __launch_bounds__(kThreads, 1)
     lvsa_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                      const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_tq,
                      const __grid_constant__ CUtensorMap tm_tk, const __grid_constant__ CUtensorMap tm_tv,
                      const AttnParams prm) {
-  using L = Smem<D, STAGES>;
+  using L = Smem<D, STAGES, kFp8>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sK = smem + L::kK;
@@ -216,13 +251,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_expect_tx(&k_full[s], L::kTile);
 #pragma unroll
         for (int c = 0; c < L::kCh; ++c)
-          tma_load_4d(sK + s * L::kTile + c * kChunk, mk, &k_full[s], c * 64, hk, ktok, b);
+          tma_load_4d(sK + s * L::kTile + c * kChunk, mk, &k_full[s], c * (128 / L::kElem), hk, ktok, b);
         if (j >= STAGES && !mbar_wait(&v_empty[s], ((j / STAGES) - 1) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT))
           break;
         mbar_expect_tx(&v_full[s], L::kTile);
 #pragma unroll
         for (int c = 0; c < L::kCh; ++c)
-          tma_load_4d(sV + s * L::kTile + c * kChunk, mv, &v_full[s], c * 64, hk, ktok, b);
+          tma_load_4d(sV + s * L::kTile + c * kChunk, mv, &v_full[s], c * (128 / L::kElem), hk, ktok, b);
         issued = j + 1;
       }
       if (*abort) {
@@ -240,15 +275,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     // consumed S(j-1), i.e. P(j-1) arrived, which iteration j-1 waited for),
     // then PV(j) once P(j) is in TMEM.
     if (lane == 0 && n > 0) {
-      constexpr uint32_t idS = idesc_f16(kBM, kBN, kBf16, false);
-      constexpr uint32_t idO = idesc_f16(kBM, D, kBf16, true);
+      // Operand format code 1 means BF16 for kind::f16 but E5M2 for kind::f8f6f4,
+      // whose E4M3 code is 0.
+      constexpr bool kFmt1 = kBf16 && !kFp8;
+      constexpr uint32_t idS = idesc_f16(kBM, kBN, kFmt1, false);
+      constexpr uint32_t idO = idesc_f16(kBM, D, kFmt1, true);
       const uint32_t k_base = smem_u32(sK), v_base = smem_u32(sV);
       auto issue_s = [&](int jj) {
         const uint32_t kb = k_base + (jj % STAGES) * L::kTile, dS = tS + (jj & 1) * 128;
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
+        for (int kk = 0; kk < D * L::kElem / 32; ++kk) {  // 32 bytes of K per instruction
           const uint32_t off = (kk >> 2) * kChunk + (kk & 3) * 32;
-          mma_ts(dS, tQ + kk * 8, sdesc_sw128(kb + off, 16, 1024), idS, kk > 0);
+          mma_ts_any<kFp8>(dS, tQ + kk * 8, sdesc_sw128(kb + off, 16, 1024), idS, kk > 0);
         }
         mma_commit(&s_full[jj & 1]);
         mma_commit(&k_empty[jj % STAGES]);
@@ -273,8 +311,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t vb = v_base + (j % STAGES) * L::kTile, pa = tP;
 #pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk)
-          mma_ts(tO, pa + kk * 8, sdesc_sw128(vb + kk * 2048, kChunk, 1024), idO, (j > 0 || kk > 0));
+        for (int kk = 0; kk < kBN * L::kElem / 32; ++kk)  // 32 / kElem keys per instruction
+          mma_ts_any<kFp8>(tO, pa + kk * 8, sdesc_sw128(vb + kk * (32 / L::kElem) * 128, kChunk, 1024), idO,
+                           (j > 0 || kk > 0));
         mma_commit(&pv_done[j & 1]);
         mma_commit(&v_empty[j % STAGES]);
       }
@@ -308,25 +347,30 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tSr = tS + lane_base + half * 64;      // my 64 S columns (buffer 0)
     const uint32_t tPr = tP + lane_base + half * 32;      // my 32 packed P columns
     const uint32_t tOr = tO + lane_base + half * (D / 2);  // my D/2 O columns
-    const float sl2 = prm.scale_log2;
+    const float sl2_base = prm.scale_log2;
+    float sq = 1.f, vref = 1.f;
+    if constexpr (kFp8) {
+      sq = text_row ? prm.tqs[(static_cast<int64_t>(b) * prm.heads + h) * prm.nqt_all + (row - prm.nqv)]
+                    : prm.qs[(static_cast<int64_t>(b) * prm.heads + h) * prm.nqv + row];
+      vref = prm.vref[static_cast<int64_t>(b) * prm.kv_heads + hk];
+    }
     if (n > 0) {
       // Query row -> TMEM: my D/2 elements as D/4 packed words at Q columns
       // [448 + half D/4, +D/4); rows past the segment are zero.
-      const uint16_t* qsrc = nullptr;
+      constexpr int kQW = D * L::kElem / 8;  // my D/2 elements as 32-bit words
+      const uint8_t* qsrc = nullptr;
       if (valid) {
-        qsrc = text_row ? reinterpret_cast<const uint16_t*>(prm.text_q) + b * prm.tq_sb +
-                              static_cast<int64_t>(tok) * prm.tq_st + h * prm.tq_sh
-                        : reinterpret_cast<const uint16_t*>(prm.q) + b * prm.q_sb +
-                              static_cast<int64_t>(tok) * prm.q_st + h * prm.q_sh;
-        qsrc += half * (D / 2);
+        const int64_t off = text_row ? b * prm.tq_sb + static_cast<int64_t>(tok) * prm.tq_st + h * prm.tq_sh
+                                     : b * prm.q_sb + static_cast<int64_t>(tok) * prm.q_st + h * prm.q_sh;
+        qsrc = reinterpret_cast<const uint8_t*>(text_row ? prm.text_q : prm.q) + (off + half * (D / 2)) * L::kElem;
       }
-      uint32_t qw[D / 4];
+      uint32_t qw[kQW];
 #pragma unroll
-      for (int i = 0; i < D / 16; ++i) {  // D/2 bf16 = D/16 16-byte words
+      for (int i = 0; i < kQW / 4; ++i) {
         const uint4 v4 = qsrc ? reinterpret_cast<const uint4*>(qsrc)[i] : make_uint4(0u, 0u, 0u, 0u);
         qw[4 * i] = v4.x; qw[4 * i + 1] = v4.y; qw[4 * i + 2] = v4.z; qw[4 * i + 3] = v4.w;
       }
-      tmem_st_q<D / 4>(tQ + lane_base + half * (D / 4), qw);
+      tmem_st_q<kQW>(tQ + lane_base + half * kQW, qw);
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(q_full);
@@ -337,6 +381,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     int kt_next = n > 0 ? prm.indices[beg] : 0;
     for (int j = 0; j < n; ++j) {
       const int flag = flag_next, kt = kt_next, bb = j & 1;
+      float sl2 = sl2_base, pscale = 1.f;  // FP8: dequantise S; fold V's tile scale into P
+      if constexpr (kFp8) {
+        const int64_t hb = static_cast<int64_t>(b) * prm.kv_heads + hk;
+        const bool tt = kt >= prm.nkv;
+        const float skj = tt ? prm.tks[hb * prm.nkt + (kt - prm.nkv)] : prm.ks[hb * prm.nkv + kt];
+        const float svj = tt ? prm.tvs[hb * prm.nkt + (kt - prm.nkv)] : prm.vs[hb * prm.nkv + kt];
+        sl2 = sl2_base * sq * skj;
+        pscale = svj / vref;
+      }
       if (j + 1 < n) {
         flag_next = prm.flags[beg + j + 1];
         kt_next = prm.indices[beg + j + 1];
@@ -396,7 +449,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float mu = (m == kNegInf) ? 0.f : m;
       const uint64_t sl2x2 = f2_pack(sl2, sl2), nmu2 = f2_pack(-mu, -mu);
       uint64_t acc2[4] = {0ull, 0ull, 0ull, 0ull};
-      uint32_t pk[32];
+      uint32_t pk[32];  // kFp8: the first 16 words hold 64 E4M3 values
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
         const uint64_t x2 = f2_fma(f2_pack(__uint_as_float(sv[2 * i]), __uint_as_float(sv[2 * i + 1])), sl2x2, nmu2);
@@ -404,7 +457,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         f2_unpack(x2, xa, xc);
         const float a = ex2_approx(xa), c = ex2_approx(xc);
         acc2[i & 3] = f2_add(acc2[i & 3], f2_pack(a, c));
-        pk[i] = pack2(a, c, kBf16);
+        if constexpr (kFp8) {
+          if (i & 1) {
+            const float a0 = __uint_as_float(pk[i - 1]), c0 = __uint_as_float(pk[i]);  // held pair i-1
+            pk[i >> 1] = pack4_e4m3(a0, c0, a * pscale, c * pscale);
+          } else {
+            pk[i] = __float_as_uint(a * pscale);
+            pk[i + 1] = __float_as_uint(c * pscale);
+          }
+        } else {
+          pk[i] = pack2(a, c, kBf16);
+        }
       }
       // The single P buffer last fed PV(j-1).
       if (j >= 1) {
@@ -412,7 +475,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                                                    LVSA_ERR_DEVICE_TIMEOUT));
         tc_fence_after();
       }
-      tmem_st32(tPr, pk);
+      if constexpr (kFp8) {
+        uint32_t pk8[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) pk8[i] = pk[i];
+        tmem_st16(tP + lane_base + half * 16, pk8);
+      } else {
+        tmem_st32(tPr, pk);
+      }
       float acc[8];
 #pragma unroll
       for (int i = 0; i < 4; ++i) f2_unpack(acc2[i], acc[2 * i], acc[2 * i + 1]);
@@ -442,7 +512,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (xchg(n & 1, l, got && !fail, l_other)) {
         const float lt = l + l_other;
         tc_fence_after();
-        const float inv = (lt > 0.f) ? 1.f / lt : 0.f;
+        const float inv = (lt > 0.f) ? vref / lt : 0.f;
 #pragma unroll
         for (int c = 0; c < D / 64; ++c) {
           uint32_t t[32];
@@ -495,12 +565,13 @@ EncodeTiledFn get_encode_fn() {
   return fn;
 }
 
-// [B, N, Hx, D] view -> 4-D map (D, Hx, N, B) with a (64, 1, 128, 1) box, 128B swizzle.
-int make_map(CUtensorMap* map, const LvsaTensor& t, int B, int N, int Hx, int D, bool bf16) {
+// [B, N, Hx, D] view -> 4-D map (D, Hx, N, B) with a (128 bytes, 1, 128, 1)
+// box, 128B swizzle.  dt: LVSA_DTYPE_BF16 / _F16 / _E4M3.
+int make_map(CUtensorMap* map, const LvsaTensor& t, int B, int N, int Hx, int D, int dt) {
   EncodeTiledFn enc = get_encode_fn();
   if (!enc) return LVSA_ERR_CUDA;
   if (!t.ptr || N < 1) return LVSA_ERR_INVALID_ARG;
-  const int64_t es = 2;
+  const int64_t es = dt == LVSA_DTYPE_E4M3 ? 1 : 2;
   if ((reinterpret_cast<uintptr_t>(t.ptr) & 15) || (t.stride_h * es) % 16 || (t.stride_t * es) % 16 ||
       (B > 1 && (t.stride_b * es) % 16))
     return LVSA_ERR_ALIGNMENT;
@@ -510,32 +581,36 @@ int make_map(CUtensorMap* map, const LvsaTensor& t, int B, int N, int Hx, int D,
   const int64_t sb = (B > 1) ? t.stride_b : t.stride_t * N;
   cuuint64_t strides[3] = {static_cast<cuuint64_t>(t.stride_h * es), static_cast<cuuint64_t>(t.stride_t * es),
                            static_cast<cuuint64_t>(sb * es)};
-  cuuint32_t box[4] = {64, 1, static_cast<cuuint32_t>(kBM), 1};
+  cuuint32_t box[4] = {static_cast<cuuint32_t>(128 / es), 1, static_cast<cuuint32_t>(kBM), 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
-  CUresult r = enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, t.ptr, dims,
+  const CUtensorMapDataType ty = dt == LVSA_DTYPE_E4M3 ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                 : dt == LVSA_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                         : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = enc(map, ty, 4, t.ptr, dims,
                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? LVSA_OK : LVSA_ERR_ALIGNMENT;
 }
 
-template <int D, int STAGES, bool kBf16>
-int launch(const LvsaAttnArgs* a, cudaStream_t stream) {
-  using L = Smem<D, STAGES>;
+template <int D, int STAGES, bool kBf16_, bool kFp8 = false>
+int launch(const LvsaAttnArgs* a, cudaStream_t stream, const LvsaFp8Scales* sc = nullptr) {
+  using L = Smem<D, STAGES, kFp8>;
   CUtensorMap mq, mk, mv, mtq, mtk, mtv;
   int st;
-  if ((st = make_map(&mq, a->q, a->batch, a->n_video, a->heads, D, kBf16))) return st;
-  if ((st = make_map(&mk, a->k, a->batch, a->n_video, a->kv_heads, D, kBf16))) return st;
-  if ((st = make_map(&mv, a->v, a->batch, a->n_video, a->kv_heads, D, kBf16))) return st;
+  const int dt = kFp8 ? LVSA_DTYPE_E4M3 : (kBf16_ ? LVSA_DTYPE_BF16 : LVSA_DTYPE_F16);
+  if ((st = make_map(&mq, a->q, a->batch, a->n_video, a->heads, D, dt))) return st;
+  if ((st = make_map(&mk, a->k, a->batch, a->n_video, a->kv_heads, D, dt))) return st;
+  if ((st = make_map(&mv, a->v, a->batch, a->n_video, a->kv_heads, D, dt))) return st;
   const bool text_rows = a->n_text > 0 && a->text_q.ptr != nullptr;
   if (a->n_text > 0) {
-    if ((st = make_map(&mtk, a->text_k, a->batch, a->n_text, a->kv_heads, D, kBf16))) return st;
-    if ((st = make_map(&mtv, a->text_v, a->batch, a->n_text, a->kv_heads, D, kBf16))) return st;
+    if ((st = make_map(&mtk, a->text_k, a->batch, a->n_text, a->kv_heads, D, dt))) return st;
+    if ((st = make_map(&mtv, a->text_v, a->batch, a->n_text, a->kv_heads, D, dt))) return st;
   } else {
     mtk = mk;
     mtv = mv;
   }
   if (text_rows) {
-    if ((st = make_map(&mtq, a->text_q, a->batch, a->n_text, a->heads, D, kBf16))) return st;
+    if ((st = make_map(&mtq, a->text_q, a->batch, a->n_text, a->heads, D, dt))) return st;
   } else {
     mtq = mq;
   }
@@ -557,8 +632,17 @@ int launch(const LvsaAttnArgs* a, cudaStream_t stream) {
   p.scale_log2 = scale * 1.4426950408889634f;
   p.frame_bits = a->frame_bits; p.indptr = a->tile_indptr; p.indices = a->tile_indices; p.flags = a->tile_flags;
   p.err = a->error_word;
+  p.qs = p.ks = p.vs = p.tqs = p.tks = p.tvs = p.vref = nullptr;
+  p.nqt_all = (a->n_text + kBlockQ - 1) / kBlockQ;
+  p.nkt = (a->n_text + kBN - 1) / kBN;
+  if (kFp8) {
+    if (!sc || !sc->q || !sc->k || !sc->v || !sc->v_ref) return LVSA_ERR_INVALID_ARG;
+    if (a->n_text > 0 && (!sc->text_k || !sc->text_v || (text_rows && !sc->text_q))) return LVSA_ERR_INVALID_ARG;
+    p.qs = sc->q; p.ks = sc->k; p.vs = sc->v; p.tqs = sc->text_q; p.tks = sc->text_k; p.tvs = sc->text_v;
+    p.vref = sc->v_ref;
+  }
 
-  auto kern = lvsa_attn_kernel<D, STAGES, kBf16>;
+  auto kern = lvsa_attn_kernel<D, STAGES, kBf16_, kFp8>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes) != cudaSuccess)
     return LVSA_ERR_CUDA;
   const int rows = text_rows ? a->n_q_tiles : a->n_q_video_tiles;
@@ -570,8 +654,9 @@ int launch(const LvsaAttnArgs* a, cudaStream_t stream) {
 }  // namespace
 }  // namespace lvsa
 
-extern "C" int lvsa_attn_fwd(const LvsaAttnArgs* a, void* stream) {
-  using namespace lvsa;
+namespace lvsa {
+namespace {
+int validate(const LvsaAttnArgs* a) {
   if (!a || !a->q.ptr || !a->k.ptr || !a->v.ptr || !a->o.ptr || !a->frame_bits || !a->tile_indptr ||
       !a->tile_indices || !a->tile_flags)
     return LVSA_ERR_INVALID_ARG;
@@ -588,6 +673,15 @@ extern "C" int lvsa_attn_fwd(const LvsaAttnArgs* a, void* stream) {
   if (a->n_text > 0 && (!a->text_k.ptr || !a->text_v.ptr)) return LVSA_ERR_INVALID_ARG;
   if (a->n_text > 0 && a->text_q.ptr && !a->text_o.ptr) return LVSA_ERR_INVALID_ARG;
   if (a->n_text > 0 && a->n_q_tiles != a->n_q_video_tiles + (a->n_text + kBlockQ - 1) / kBlockQ) return LVSA_ERR_GEOMETRY;
+  return LVSA_OK;
+}
+}  // namespace
+}  // namespace lvsa
+
+extern "C" int lvsa_attn_fwd(const LvsaAttnArgs* a, void* stream) {
+  using namespace lvsa;
+  const int v = validate(a);
+  if (v != LVSA_OK) return v;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool bf16 = a->dtype == LVSA_DTYPE_BF16;
   if (a->dtype != LVSA_DTYPE_BF16 && a->dtype != LVSA_DTYPE_F16) return LVSA_ERR_UNSUPPORTED;
@@ -596,6 +690,17 @@ extern "C" int lvsa_attn_fwd(const LvsaAttnArgs* a, void* stream) {
     case 64: return bf16 ? launch<64, 6, true>(a, s) : launch<64, 6, false>(a, s);
     default: return LVSA_ERR_UNSUPPORTED;
   }
+}
+
+extern "C" int lvsa_attn_fwd_fp8(const LvsaAttnArgs* a, const LvsaFp8Scales* sc, void* stream) {
+  using namespace lvsa;
+  const int v = validate(a);
+  if (v != LVSA_OK) return v;
+  if (!sc) return LVSA_ERR_INVALID_ARG;
+  if (a->head_dim != 128) return LVSA_ERR_UNSUPPORTED;
+  if (a->dtype != LVSA_DTYPE_BF16 && a->dtype != LVSA_DTYPE_F16) return LVSA_ERR_UNSUPPORTED;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return a->dtype == LVSA_DTYPE_BF16 ? launch<128, 6, true, true>(a, s, sc) : launch<128, 6, false, true>(a, s, sc);
 }
 
 extern "C" const char* lvsa_status_str(int status) {
