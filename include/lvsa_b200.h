@@ -160,6 +160,34 @@ typedef struct LvsaFp8Scales {
  * `dtype` naming the OUTPUT type (bf16 or f16).  head_dim 128 only. */
 int lvsa_attn_fwd_fp8(const LvsaAttnArgs* args, const LvsaFp8Scales* scales, void* stream);
 
+/* FP8 attention that allocates no device memory.  No counterpart in the
+ * reference: an addition of this library.
+ *
+ * For callers that cannot call cudaMalloc on this path: serving runtimes
+ * whose device memory is a fixed pool owned by their own allocator, hosts
+ * that bind this library from a language runtime with no CUDA allocator,
+ * and loops that must keep a constant memory footprint.  Arguments are those
+ * of lvsa_attn_fwd (bf16/f16 q, k, v and optional text inputs, outputs, the
+ * tile CSR); the inputs are quantised to E4M3 into a scratch array owned by
+ * the library, then the lvsa_attn_fwd_fp8 kernel runs on them.
+ *
+ *  - Limit: LVSA_NOALLOC_SCRATCH_BYTES (96 MiB) of scratch, which every GPU
+ *    that loads the library holds until the process exits.  A call needs the
+ *    E4M3 copies of q, k, v (+ text q, k, v), one fp32 scale per 128-token
+ *    tile and head of each, and one fp32 per batch and K/V head, each part
+ *    rounded up to 256 bytes; a larger call returns LVSA_ERR_CAPACITY and
+ *    launches nothing.
+ *  - The first call on a device looks up the array's device address with
+ *    that device current; make that first call before any stream capture.
+ *  - All calls share the one array and it keeps the previous call's
+ *    contents; the part that must start at zero (the per-head V reference)
+ *    is cleared by each call.  Calls that overlap on the GPU (different
+ *    streams, or host threads on one device) race on the array: the caller
+ *    must serialise them.
+ *  - head_dim 128 only, as lvsa_attn_fwd_fp8. */
+#define LVSA_NOALLOC_SCRATCH_BYTES (96u * 1024u * 1024u)
+int lvsa_attn_fwd_fp8_noalloc(const LvsaAttnArgs* args, void* stream);
+
 /* Human-readable name of a status code. */
 const char* lvsa_status_str(int status);
 

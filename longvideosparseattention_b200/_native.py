@@ -27,7 +27,8 @@ LVSA_DTYPE_F16 = 1
 LVSA_MAX_FRAMES = 2048
 
 EXPORTED_SYMBOLS = ("lvsa_mask_layout", "lvsa_build_mask", "lvsa_attn_fwd", "lvsa_quantize_e4m3",
-                    "lvsa_attn_fwd_fp8", "lvsa_status_str", "lvsa_abi_version")
+                    "lvsa_attn_fwd_fp8", "lvsa_attn_fwd_fp8_noalloc", "lvsa_status_str",
+                    "lvsa_abi_version")
 LVSA_DTYPE_E4M3 = 2
 
 _i32, _i64, _vp = ctypes.c_int32, ctypes.c_int64, ctypes.c_void_p
@@ -106,6 +107,8 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
         lib.lvsa_quantize_e4m3.restype = ctypes.c_int
         lib.lvsa_attn_fwd_fp8.argtypes = [ctypes.POINTER(LvsaAttnArgs), ctypes.POINTER(LvsaFp8Scales), _vp]
         lib.lvsa_attn_fwd_fp8.restype = ctypes.c_int
+        lib.lvsa_attn_fwd_fp8_noalloc.argtypes = [ctypes.POINTER(LvsaAttnArgs), _vp]
+        lib.lvsa_attn_fwd_fp8_noalloc.restype = ctypes.c_int
         lib.lvsa_status_str.argtypes = [ctypes.c_int]
         lib.lvsa_status_str.restype = ctypes.c_char_p
         lib.lvsa_abi_version.argtypes = []

@@ -169,3 +169,20 @@ def test_mask_layout_host_call_and_errors():
         mask_layout(9, 16, 1, 1, 4, block_q=100)
     with pytest.raises(AssertionError):
         mask_layout(N.LVSA_MAX_FRAMES + 1, 4, 1, 1, 4)
+
+
+def test_noalloc_entry_rejects_oversize_before_any_cuda_call():
+    """The fixed-scratch FP8 entry checks its limit before touching CUDA, so
+    this runs without a GPU; the pointers are never dereferenced."""
+    import ctypes
+    from longvideosparseattention_b200 import _native as N
+    lib = N.load()
+    fake = N.LvsaTensor(16, 0, 0, 0)
+    a = N.LvsaAttnArgs()
+    a.q = a.k = a.v = a.o = fake
+    a.batch, a.n_video, a.n_text, a.heads, a.kv_heads, a.head_dim, a.dtype = 1, 126360, 0, 12, 12, 128, 0
+    # E4M3 q, k and v alone: 3 x 126360 x 12 x 128 bytes = 582 MB > 96 MiB
+    assert lib.lvsa_attn_fwd_fp8_noalloc(ctypes.byref(a), None) == N.LVSA_ERR_CAPACITY
+    a.head_dim = 64
+    assert lib.lvsa_attn_fwd_fp8_noalloc(ctypes.byref(a), None) == N.LVSA_ERR_UNSUPPORTED
+    assert lib.lvsa_attn_fwd_fp8_noalloc(None, None) == N.LVSA_ERR_INVALID_ARG
