@@ -1,26 +1,31 @@
 // Block-sparse LVSA attention forward for sm_100a (tcgen05 + TMEM + TMA).
 //
 // One CTA per (128-row query tile, head, batch); 320 threads:
-//   warps 0-7  softmax, two warps per query row: warp w owns key columns
-//              [64 (w / 4), +64) of rows 32 (w % 4) + lane (= TMEM lanes).
-//              The pair exchanges its partial row max through shared memory,
-//              then each warp applies the in-tile frame mask (flagged tiles
-//              only), exponentiates its 64 columns (log2 domain, lazy O
-//              rescale) and packs P to bf16/f16 into TMEM.
-//              Before the loop the same warps copy the query tile from global
-//              memory into TMEM (bf16 pairs, lane = row).
-//   warp 8     TMA producer: K and V tiles of the row's CSR list, read in
-//              place from the [B, N, H, D] tensors into a 3-stage (D=128) /
-//              6-stage (D=64) ring; K and V stages are released separately.
-//   warp 9     TMEM allocator + single-thread tcgen05.mma issuer:
-//              S(j+1) = Q K_{j+1}^T (A = Q from TMEM, B = K from shared memory,
-//              N = 128) is issued before O += P(j) V_j (A = P from TMEM), so the
-//              tensor pipe computes the next scores while the softmax works on
-//              the current ones.  With both A operands in TMEM the MMAs read only
-//              K and V from shared memory, which keeps its bandwidth for TMA.
-// TMEM columns: S0 [0,128) S1 [128,256) O [256,256+D) P [384,448)
-// Q [448, 448+D/2): S is double-buffered, so no MMA waits on the softmax of
-// the tile it is not consuming.
+//   warps 0-7  softmax, one thread per query row and key-tile class: warps
+//              0-3 take the even entries j of the row's tile list, warps 4-7
+//              the odd ones (warp w reads TMEM lanes 32 (w % 4) .. +32, so a
+//              row's two threads sit on the same SM sub-partition).  Each
+//              class keeps its own running max / sum and its own O
+//              accumulator, so the two warps of a sub-partition never wait
+//              for each other inside the loop: while one exponentiates (MUFU),
+//              the other loads, masks and reduces.  The two partial results
+//              are merged once, in the epilogue.
+//   warp 8     TMA producer: the query tile once, then K and V tiles of the
+//              row's CSR list, read in place from the [B, N, H, D] tensors
+//              into a ring of shared-memory stages (K and V released
+//              separately).
+//   warp 9     TMEM allocator + single-thread tcgen05.mma issuer, in the
+//              order S(0) S(1) PV(0) S(2) PV(1) S(3) ...:  S(j) = Q K_j^T
+//              (both operands in shared memory) into S buffer j % 2; PV(j)
+//              = P(j) V_j accumulates into O buffer j % 2 with P read from
+//              the same TMEM columns that held S(j).  S(j+2) reuses that
+//              buffer and is issued after PV(j); tcgen05.mma operations of one
+//              thread execute in issue order.
+// TMEM columns: S/P buffer c at [128 c, 128 c + 128), O buffer c at
+// [256 + 128 c, 256 + 128 c + D).  Per key tile the softmax thread loads S
+// columns [0,64), then [64,128) (row max), writes P of keys 0-63 into
+// columns [0,32) (bf16 pairs; E4M3 quads: [0,16)), reloads [64,128) and
+// writes P of keys 64-127 after it.
 //
 // Semantics follow lvsa_sdpa (lvsa/sparse_attention.py:643-706) with the
 // processor's text handling (lvsa/lvsa_processor.py:545-549, 584-591):
@@ -83,18 +88,21 @@ struct AttnParams {
   int nqt_all, nkt;  // query / key tiles of the text segment
 };
 
+
 template <int D, int STAGES, bool kFp8 = false>
 struct Smem {
   static constexpr int kElem = kFp8 ? 1 : 2;       // bytes per element
   static constexpr int kCh = D * kElem / 128;      // 128-byte column slabs per row
   static constexpr int kTile = kCh * kChunk;       // bytes of one 128 x D tile
-  static constexpr int kK = 0;
+  static constexpr int kQ = 0;                     // query tile; the epilogue's merge buffer afterwards
+  static constexpr int kK = kQ + kTile;
   static constexpr int kV = kK + STAGES * kTile;
   static constexpr int kBar = kV + STAGES * kTile;
-  static constexpr int kNumBars = 1 + 4 * STAGES + 6 + 1;
+  static constexpr int kNumBars = 4 * STAGES + 8;
   static constexpr int kMisc = kBar + kNumBars * 8;
-  static constexpr int kRed = kMisc + 16;          // pair exchange: [2 parity][2 half][128 rows] f32 + i32
-  static constexpr int kBytes = kRed + 2 * 2 * 2 * kBM * 4 + 1024;  // + alignment slack
+  static constexpr int kBytes = kMisc + 16 + 1024;  // + alignment slack
+  static_assert(kBytes <= 232448, "shared memory");
+  static_assert(2 * 2 * kBM * 4 <= kTile, "merge buffer fits in the query tile");
 };
 
 __device__ __forceinline__ uint32_t pack2(float a, float b, bool bf16) {
@@ -138,16 +146,6 @@ __device__ __forceinline__ void tile_mask(uint32_t (&am)[4], const AttnParams& p
   }
 }
 
-template <int N>
-__device__ __forceinline__ void tmem_st_q(uint32_t taddr, const uint32_t (&r)[N]) {
-  if constexpr (N == 32) {
-    tmem_st32(taddr, r);
-  } else {
-    static_assert(N == 16, "head_dim 64 or 128");
-    tmem_st16(taddr, r);
-  }
-}
-
 // tcgen05.mma kind::f8f6f4 (E4M3 x E4M3 -> fp32), A from TMEM.
 __device__ __forceinline__ void mma_ts_f8(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t idesc, uint32_t acc) {
   asm volatile(
@@ -170,6 +168,112 @@ __device__ __forceinline__ uint32_t pack4_e4m3(float a, float b, float c, float 
   return static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
 }
 
+
+// tcgen05.mma kind::f8f6f4, both operands in shared memory.
+__device__ __forceinline__ void mma_ss_f8(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+template <bool kFp8>
+__device__ __forceinline__ void mma_ss_any(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  if constexpr (kFp8) mma_ss_f8(d, a, b, idesc, acc);
+  else mma_ss(d, a, b, idesc, acc);
+}
+
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// Sets masked-out columns of one 64-column half to -inf (bits of w0 | w1 << 32).
+__device__ __forceinline__ void mask64(uint32_t (&sv)[64], uint32_t w0, uint32_t w1) {
+#pragma unroll
+  for (int i = 0; i < 64; ++i)
+    if (!((((i < 32) ? w0 : w1) >> (i & 31)) & 1u)) sv[i] = __float_as_uint(kNegInf);
+}
+
+__device__ __forceinline__ void mask32(uint32_t (&sv)[32], uint32_t w) {
+#pragma unroll
+  for (int i = 0; i < 32; ++i)
+    if (!((w >> i) & 1u)) sv[i] = __float_as_uint(kNegInf);
+}
+
+__device__ __forceinline__ float max64(const uint32_t (&sv)[64]) {
+  float mx[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) mx[i] = fmax3(__uint_as_float(sv[i]), __uint_as_float(sv[8 + i]), __uint_as_float(sv[16 + i]));
+#pragma unroll
+  for (int i = 0; i < 8; ++i) mx[i] = fmax3(mx[i], __uint_as_float(sv[24 + i]), __uint_as_float(sv[32 + i]));
+#pragma unroll
+  for (int i = 0; i < 8; ++i) mx[i] = fmax3(mx[i], __uint_as_float(sv[40 + i]), __uint_as_float(sv[48 + i]));
+#pragma unroll
+  for (int i = 0; i < 8; ++i) mx[i] = fmaxf(mx[i], __uint_as_float(sv[56 + i]));
+  return fmaxf(fmax3(mx[0], mx[1], mx[2]), fmax3(fmax3(mx[3], mx[4], mx[5]), mx[6], mx[7]));
+}
+
+__device__ __forceinline__ float max32(const uint32_t (&sv)[32]) {
+  float mx[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) mx[i] = fmax3(__uint_as_float(sv[i]), __uint_as_float(sv[4 + i]), __uint_as_float(sv[8 + i]));
+#pragma unroll
+  for (int k = 12; k < 28; k += 8)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) mx[i] = fmax3(mx[i], __uint_as_float(sv[k + i]), __uint_as_float(sv[k + 4 + i]));
+#pragma unroll
+  for (int i = 0; i < 4; ++i) mx[i] = fmaxf(mx[i], __uint_as_float(sv[28 + i]));
+  return fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+}
+
+// P = 2^(s * sl2 - mu) for 64 key columns, packed for the PV MMA: bf16/f16
+// pairs (32 words) or, with kFp8, E4M3 quads of P * pscale (words 0-15).
+// Returns the row sum of the unscaled P.
+template <bool kBf16, bool kFp8>
+__device__ __forceinline__ float exp64(const uint32_t (&sv)[64], uint64_t sl2x2, uint64_t nmu2, float pscale,
+                                       uint32_t (&pk)[32]) {
+  uint64_t acc2[4] = {0ull, 0ull, 0ull, 0ull};
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const uint64_t x2 = f2_fma(f2_pack(__uint_as_float(sv[2 * i]), __uint_as_float(sv[2 * i + 1])), sl2x2, nmu2);
+    float xa, xc;
+    f2_unpack(x2, xa, xc);
+    const float a = ex2_approx(xa), c = ex2_approx(xc);
+    acc2[i & 3] = f2_add(acc2[i & 3], f2_pack(a, c));
+    if constexpr (kFp8) {
+      if (i & 1) {
+        const float a0 = __uint_as_float(pk[i - 1]), c0 = __uint_as_float(pk[i]);  // held pair i-1
+        pk[i >> 1] = pack4_e4m3(a0, c0, a * pscale, c * pscale);
+      } else {
+        pk[i] = __float_as_uint(a * pscale);
+        pk[i + 1] = __float_as_uint(c * pscale);
+      }
+    } else {
+      pk[i] = pack2(a, c, kBf16);
+    }
+  }
+  float acc[8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) f2_unpack(acc2[i], acc[2 * i], acc[2 * i + 1]);
+  return ((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7]));
+}
+
+template <bool kFp8>
+__device__ __forceinline__ void store_p(uint32_t taddr, const uint32_t (&pk)[32]) {
+  if constexpr (kFp8) {
+    uint32_t pk8[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) pk8[i] = pk[i];
+    tmem_st16(taddr, pk8);
+  } else {
+    tmem_st32(taddr, pk);
+  }
+}
+
 // kBf16: type of O (and of Q/K/V unless kFp8).  kFp8: Q/K/V are E4M3 copies
 // with per-tile scales (QK^T and PV on kind::f8f6f4, P rounded to E4M3).
 template <int D, int STAGES, bool kBf16, bool kFp8 = false>
@@ -181,6 +285,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   using L = Smem<D, STAGES, kFp8>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem + L::kQ;
   uint8_t* sK = smem + L::kK;
   uint8_t* sV = smem + L::kV;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBar);
@@ -189,10 +294,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* v_full = k_full + STAGES;
   uint64_t* k_empty = v_full + STAGES;   // K stage free: the S of its tile is done
   uint64_t* v_empty = k_empty + STAGES;  // V stage free: the PV of its tile is done
-  uint64_t* s_full = v_empty + STAGES;   // [2] S buffer b holds S(j), j % 2 == b
-  uint64_t* p_full = s_full + 2;         // [2] P buffer b written (and S buffer b read)
-  uint64_t* pv_done = p_full + 2;        // [2] PV(j) done, j % 2 == b
-  uint64_t* drain = pv_done + 2;
+  uint64_t* s_full = v_empty + STAGES;   // [2] S buffer c holds S(j), j % 2 == c
+  uint64_t* p_full = s_full + 2;         // [2] P(j) written into buffer c
+  uint64_t* o_done = p_full + 2;         // every MMA of the CTA retired
+  uint64_t* drain = o_done + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMisc);
   volatile int* abort = reinterpret_cast<volatile int*>(smem + L::kMisc + 4);
   volatile int* never = reinterpret_cast<volatile int*>(smem + L::kMisc + 8);  // stays 0: drain waits
@@ -206,7 +311,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int hk = h / (prm.heads / prm.kv_heads);
 
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 2 * 128);  // the softmax threads' copies of Q into TMEM
+    mbar_init(q_full, 1);
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&v_full[s], 1);
@@ -215,9 +320,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 2 * 128);
-      mbar_init(&pv_done[i], 1);
+      mbar_init(&p_full[i], 128);
     }
+    mbar_init(o_done, 1);
     mbar_init(drain, 1);
     *abort = 0;
     *never = 0;
@@ -231,14 +336,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tS = tmem, tO = tmem + 256, tP = tmem + 384, tQ = tmem + 448;
+  const uint32_t tS = tmem, tO = tmem + 256;
 
   if (warp == kProducerWarp) {
     // ---------------------------------------------------------- producer
     if (lane == 0 && n > 0) {
+      const CUtensorMap* mq = text_row ? &tm_tq : &tm_q;
+      tma_prefetch_desc(mq);
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
-      int issued = 0;
+      mbar_expect_tx(q_full, L::kTile);
+#pragma unroll
+      for (int c = 0; c < L::kCh; ++c) tma_load_4d(sQ + c * kChunk, mq, q_full, c * (128 / L::kElem), h, tok0, b);
+      int k_issued = 0, v_issued = 0;
       for (int j = 0; j < n; ++j) {
         const int s = j % STAGES;
         const int kt = prm.indices[beg + j];
@@ -252,41 +362,39 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int c = 0; c < L::kCh; ++c)
           tma_load_4d(sK + s * L::kTile + c * kChunk, mk, &k_full[s], c * (128 / L::kElem), hk, ktok, b);
+        k_issued = j + 1;
         if (j >= STAGES && !mbar_wait(&v_empty[s], ((j / STAGES) - 1) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT))
           break;
         mbar_expect_tx(&v_full[s], L::kTile);
 #pragma unroll
         for (int c = 0; c < L::kCh; ++c)
           tma_load_4d(sV + s * L::kTile + c * kChunk, mv, &v_full[s], c * (128 / L::kElem), hk, ktok, b);
-        issued = j + 1;
+        v_issued = j + 1;
       }
       if (*abort) {
         // Drain our own copies still in flight before the CTA retires.
-        for (int j = max(0, issued - STAGES); j < issued; ++j) {
-          const int s = j % STAGES;
-          mbar_wait(&k_full[s], (j / STAGES) & 1, never, nullptr, 0);
-          mbar_wait(&v_full[s], (j / STAGES) & 1, never, nullptr, 0);
-        }
+        mbar_wait(q_full, 0, never, nullptr, 0);
+        for (int j = max(0, k_issued - STAGES); j < k_issued; ++j)
+          mbar_wait(&k_full[j % STAGES], (j / STAGES) & 1, never, nullptr, 0);
+        for (int j = max(0, v_issued - STAGES); j < v_issued; ++j)
+          mbar_wait(&v_full[j % STAGES], (j / STAGES) & 1, never, nullptr, 0);
       }
     }
   } else if (warp == kMmaWarp) {
     // ---------------------------------------------------------- MMA issuer
-    // Iteration j: S(j+1) into S buffer (j+1)%2 (free once the softmax has
-    // consumed S(j-1), i.e. P(j-1) arrived, which iteration j-1 waited for),
-    // then PV(j) once P(j) is in TMEM.
     if (lane == 0 && n > 0) {
       // Operand format code 1 means BF16 for kind::f16 but E5M2 for kind::f8f6f4,
       // whose E4M3 code is 0.
       constexpr bool kFmt1 = kBf16 && !kFp8;
       constexpr uint32_t idS = idesc_f16(kBM, kBN, kFmt1, false);
       constexpr uint32_t idO = idesc_f16(kBM, D, kFmt1, true);
-      const uint32_t k_base = smem_u32(sK), v_base = smem_u32(sV);
+      const uint32_t q_base = smem_u32(sQ), k_base = smem_u32(sK), v_base = smem_u32(sV);
       auto issue_s = [&](int jj) {
         const uint32_t kb = k_base + (jj % STAGES) * L::kTile, dS = tS + (jj & 1) * 128;
 #pragma unroll
-        for (int kk = 0; kk < D * L::kElem / 32; ++kk) {  // 32 bytes of K per instruction
+        for (int kk = 0; kk < D * L::kElem / 32; ++kk) {  // 32 bytes of Q and K per instruction
           const uint32_t off = (kk >> 2) * kChunk + (kk & 3) * 32;
-          mma_ts_any<kFp8>(dS, tQ + kk * 8, sdesc_sw128(kb + off, 16, 1024), idS, kk > 0);
+          mma_ss_any<kFp8>(dS, sdesc_sw128(q_base + off, 16, 1024), sdesc_sw128(kb + off, 16, 1024), idS, kk > 0);
         }
         mma_commit(&s_full[jj & 1]);
         mma_commit(&k_empty[jj % STAGES]);
@@ -297,56 +405,48 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         issue_s(0);
       }
+      if (ok && n > 1 && (ok = mbar_wait(&k_full[1 % STAGES], (1 / STAGES) & 1, abort, prm.err,
+                                         LVSA_ERR_DEVICE_TIMEOUT))) {
+        tc_fence_after();
+        issue_s(1);
+      }
       for (int j = 0; ok && j < n; ++j) {
-        if (j + 1 < n) {
-          // S buffer (j+1)%2 last held S(j-1): P(j-1) arrived before PV(j-1) was issued.
-          if (!(ok = mbar_wait(&k_full[(j + 1) % STAGES], ((j + 1) / STAGES) & 1, abort, prm.err,
+        const int c = j & 1, it = j >> 1;
+        if (!(ok = mbar_wait(&p_full[c], it & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT))) break;
+        if (!(ok = mbar_wait(&v_full[j % STAGES], (j / STAGES) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT))) break;
+        tc_fence_after();
+        const uint32_t vb = v_base + (j % STAGES) * L::kTile, pa = tS + c * 128, dO = tO + c * 128;
+#pragma unroll
+        for (int kk = 0; kk < kBN * L::kElem / 32; ++kk)  // 32 / kElem keys per instruction
+          mma_ts_any<kFp8>(dO, pa + kk * 8, sdesc_sw128(vb + kk * (32 / L::kElem) * 128, kChunk, 1024), idO,
+                           (it > 0 || kk > 0));
+        mma_commit(&v_empty[j % STAGES]);
+        if (j + 2 < n) {
+          // S buffer c: P(j) was read by PV(j), issued just before.
+          if (!(ok = mbar_wait(&k_full[(j + 2) % STAGES], ((j + 2) / STAGES) & 1, abort, prm.err,
                                LVSA_ERR_DEVICE_TIMEOUT)))
             break;
           tc_fence_after();
-          issue_s(j + 1);
+          issue_s(j + 2);
         }
-        if (!(ok = mbar_wait(&p_full[j & 1], (j >> 1) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT))) break;
-        if (!(ok = mbar_wait(&v_full[j % STAGES], (j / STAGES) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT))) break;
-        tc_fence_after();
-        const uint32_t vb = v_base + (j % STAGES) * L::kTile, pa = tP;
-#pragma unroll
-        for (int kk = 0; kk < kBN * L::kElem / 32; ++kk)  // 32 / kElem keys per instruction
-          mma_ts_any<kFp8>(tO, pa + kk * 8, sdesc_sw128(vb + kk * (32 / L::kElem) * 128, kChunk, 1024), idO,
-                           (j > 0 || kk > 0));
-        mma_commit(&pv_done[j & 1]);
-        mma_commit(&v_empty[j % STAGES]);
       }
+      if (ok) mma_commit(o_done);
       // Make sure every MMA this thread issued has retired before TMEM is freed.
       mma_commit(drain);
       mbar_wait(drain, 0, never, nullptr, 0);
     }
   } else {
     // ---------------------------------------------------------- softmax
-    const int half = warp >> 2;                  // key columns [64 half, 64 half + 64)
+    const int cls = warp >> 2;                   // tile-list entries j with j % 2 == cls
     const int r = ((warp & 3) << 5) | lane;      // query row = TMEM lane
-    const uint32_t pair_bar = 1 + (warp & 3);    // named barrier shared with the partner warp
-    float* red_max = reinterpret_cast<float*>(smem + L::kRed);           // [2][2][128]
-    int* red_ok = reinterpret_cast<int*>(smem + L::kRed + 2 * 2 * kBM * 4);
-    // Exchange one value with the partner warp (same rows, other 64 columns).
-    // Both warps see the same (mine, theirs) flags and take the same branch.
-    auto xchg = [&](int par, float v, bool mine, float& other) -> bool {
-      red_max[(par * 2 + half) * kBM + r] = v;
-      red_ok[(par * 2 + half) * kBM + r] = mine ? 1 : 0;
-      asm volatile("bar.sync %0, 64;" ::"r"(pair_bar) : "memory");
-      other = red_max[(par * 2 + (half ^ 1)) * kBM + r];
-      const bool theirs = red_ok[(par * 2 + (half ^ 1)) * kBM + r] != 0;
-      return __all_sync(0xFFFFFFFFu, mine && theirs);
-    };
+    const uint32_t pair_bar = 1 + (warp & 3);    // named barrier shared with the other class's warp
     const int seg_len = text_row ? prm.n_text : prm.n_video;
     const int tok = tok0 + r;
     const bool valid = tok < seg_len;
     const int fq = text_row ? 0 : min(tok / prm.P, prm.T - 1);
     const uint32_t* fbits = prm.frame_bits + static_cast<size_t>(fq) * prm.words;
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    const uint32_t tSr = tS + lane_base + half * 64;      // my 64 S columns (buffer 0)
-    const uint32_t tPr = tP + lane_base + half * 32;      // my 32 packed P columns
-    const uint32_t tOr = tO + lane_base + half * (D / 2);  // my D/2 O columns
+    const uint32_t tSc = tS + cls * 128 + lane_base;  // my S / P buffer
     const float sl2_base = prm.scale_log2;
     float sq = 1.f, vref = 1.f;
     if constexpr (kFp8) {
@@ -354,33 +454,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                     : prm.qs[(static_cast<int64_t>(b) * prm.heads + h) * prm.nqv + row];
       vref = prm.vref[static_cast<int64_t>(b) * prm.kv_heads + hk];
     }
-    if (n > 0) {
-      // Query row -> TMEM: my D/2 elements as D/4 packed words at Q columns
-      // [448 + half D/4, +D/4); rows past the segment are zero.
-      constexpr int kQW = D * L::kElem / 8;  // my D/2 elements as 32-bit words
-      const uint8_t* qsrc = nullptr;
-      if (valid) {
-        const int64_t off = text_row ? b * prm.tq_sb + static_cast<int64_t>(tok) * prm.tq_st + h * prm.tq_sh
-                                     : b * prm.q_sb + static_cast<int64_t>(tok) * prm.q_st + h * prm.q_sh;
-        qsrc = reinterpret_cast<const uint8_t*>(text_row ? prm.text_q : prm.q) + (off + half * (D / 2)) * L::kElem;
-      }
-      uint32_t qw[kQW];
-#pragma unroll
-      for (int i = 0; i < kQW / 4; ++i) {
-        const uint4 v4 = qsrc ? reinterpret_cast<const uint4*>(qsrc)[i] : make_uint4(0u, 0u, 0u, 0u);
-        qw[4 * i] = v4.x; qw[4 * i + 1] = v4.y; qw[4 * i + 2] = v4.z; qw[4 * i + 3] = v4.w;
-      }
-      tmem_st_q<kQW>(tQ + lane_base + half * kQW, qw);
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(q_full);
-    }
+    constexpr int kPHalf = kFp8 ? 16 : 32;  // TMEM columns of P for 64 keys
     float m = kNegInf, l = 0.f;
-    bool ok = true, fail = false;  // fail: a wait below timed out; reported at the next exchange
-    int flag_next = n > 0 ? prm.flags[beg] : 0;
-    int kt_next = n > 0 ? prm.indices[beg] : 0;
-    for (int j = 0; j < n; ++j) {
-      const int flag = flag_next, kt = kt_next, bb = j & 1;
+    bool ok = true;
+    int flag_next = cls < n ? prm.flags[beg + cls] : 0;
+    int kt_next = cls < n ? prm.indices[beg + cls] : 0;
+    for (int j = cls, it = 0; j < n; j += 2, ++it) {
+      const int flag = flag_next, kt = kt_next;
+      if (j + 2 < n) {
+        flag_next = prm.flags[beg + j + 2];
+        kt_next = prm.indices[beg + j + 2];
+      }
       float sl2 = sl2_base, pscale = 1.f;  // FP8: dequantise S; fold V's tile scale into P
       if constexpr (kFp8) {
         const int64_t hb = static_cast<int64_t>(b) * prm.kv_heads + hk;
@@ -390,108 +474,64 @@ __global__ void __launch_bounds__(kThreads, 1)
         sl2 = sl2_base * sq * skj;
         pscale = svj / vref;
       }
-      if (j + 1 < n) {
-        flag_next = prm.flags[beg + j + 1];
-        kt_next = prm.indices[beg + j + 1];
+      uint32_t am[4] = {~0u, ~0u, ~0u, ~0u};
+      if (flag) tile_mask(am, prm, kt, text_row, fbits);
+      if (!__all_sync(0xFFFFFFFFu, mbar_wait(&s_full[cls], it & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT))) {
+        ok = false;
+        break;
       }
-      const bool got =
-          __all_sync(0xFFFFFFFFu, mbar_wait(&s_full[bb], (j >> 1) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT));
+      tc_fence_after();
       uint32_t sv[64];
-      float pm = kNegInf;
-      if (got) {
-        tc_fence_after();
-        tmem_ld64(tSr + bb * 128, sv);
-        if (flag) {
-          uint32_t am[4];
-          tile_mask(am, prm, kt, text_row, fbits);
-#pragma unroll
-          for (int i = 0; i < 64; ++i)
-            if (!((am[2 * half + (i >> 5)] >> (i & 31)) & 1u)) sv[i] = __float_as_uint(kNegInf);
-        }
-        float mx8[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) mx8[i] = __uint_as_float(sv[i]);
-#pragma unroll
-        for (int i = 8; i < 64; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], __uint_as_float(sv[i]));
-#pragma unroll
-        for (int w = 4; w >= 1; w >>= 1)
-#pragma unroll
-          for (int i = 0; i < w; ++i) mx8[i] = fmaxf(mx8[i], mx8[i + w]);
-        pm = mx8[0];
+      tmem_ld64(tSc, sv);  // keys 0-63
+      float mx_hi;
+      {
+        uint32_t t[32];
+        tmem_ld32(tSc + 64, t);
+        if (flag) mask32(t, am[2]);
+        mx_hi = max32(t);
+        tmem_ld32(tSc + 96, t);
+        if (flag) mask32(t, am[3]);
+        mx_hi = fmaxf(mx_hi, max32(t));
       }
-      float other;
-      ok = xchg(bb, pm, got && !fail, other);
-      if (!ok) break;
-      const float m_new = fmaxf(m, fmaxf(pm, other) * sl2);
-      if (j == 0) {
-        m = m_new;
+      if (flag) mask64(sv, am[0], am[1]);
+      const float m_new = fmaxf(m, fmaxf(max64(sv), mx_hi) * sl2);
+      if (it == 0) {
+        m = m_new;  // my O buffer has not been written yet
       } else {
-        // Lazy rescale of my half of O (both warps of the pair decide alike).
+        // Lazy rescale of my O buffer.  It last received PV(j-2), which was
+        // issued before S(j): the s_full commit above covers it.
         const bool need = m_new > m + kRescaleThreshold;
         if (__any_sync(0xFFFFFFFFu, need)) {
-          // O must hold PV(j-1) completely before it is scaled.
-          fail |= !__all_sync(0xFFFFFFFFu, mbar_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, abort,
-                                                     prm.err, LVSA_ERR_DEVICE_TIMEOUT));
-          tc_fence_after();
           const float alpha = need ? ex2_approx(m - m_new) : 1.f;
           if (need) m = m_new;
+          const uint32_t tOc = tO + cls * 128 + lane_base;
 #pragma unroll
-          for (int c = 0; c < D / 64; ++c) {
+          for (int c = 0; c < D / 32; ++c) {
             uint32_t t[32];
-            tmem_ld32(tOr + c * 32, t);
+            tmem_ld32(tOc + c * 32, t);
 #pragma unroll
             for (int i = 0; i < 32; ++i) t[i] = __float_as_uint(__uint_as_float(t[i]) * alpha);
-            tmem_st32(tOr + c * 32, t);
+            tmem_st32(tOc + c * 32, t);
           }
           l *= alpha;
         }
       }
       const float mu = (m == kNegInf) ? 0.f : m;
       const uint64_t sl2x2 = f2_pack(sl2, sl2), nmu2 = f2_pack(-mu, -mu);
-      uint64_t acc2[4] = {0ull, 0ull, 0ull, 0ull};
-      uint32_t pk[32];  // kFp8: the first 16 words hold 64 E4M3 values
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const uint64_t x2 = f2_fma(f2_pack(__uint_as_float(sv[2 * i]), __uint_as_float(sv[2 * i + 1])), sl2x2, nmu2);
-        float xa, xc;
-        f2_unpack(x2, xa, xc);
-        const float a = ex2_approx(xa), c = ex2_approx(xc);
-        acc2[i & 3] = f2_add(acc2[i & 3], f2_pack(a, c));
-        if constexpr (kFp8) {
-          if (i & 1) {
-            const float a0 = __uint_as_float(pk[i - 1]), c0 = __uint_as_float(pk[i]);  // held pair i-1
-            pk[i >> 1] = pack4_e4m3(a0, c0, a * pscale, c * pscale);
-          } else {
-            pk[i] = __float_as_uint(a * pscale);
-            pk[i + 1] = __float_as_uint(c * pscale);
-          }
-        } else {
-          pk[i] = pack2(a, c, kBf16);
-        }
-      }
-      // The single P buffer last fed PV(j-1).
-      if (j >= 1) {
-        fail |= !__all_sync(0xFFFFFFFFu, mbar_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, abort, prm.err,
-                                                   LVSA_ERR_DEVICE_TIMEOUT));
-        tc_fence_after();
-      }
-      if constexpr (kFp8) {
-        uint32_t pk8[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) pk8[i] = pk[i];
-        tmem_st16(tP + lane_base + half * 16, pk8);
-      } else {
-        tmem_st32(tPr, pk);
-      }
-      float acc[8];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) f2_unpack(acc2[i], acc[2 * i], acc[2 * i + 1]);
-      l += ((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7]));
+      uint32_t pk[32];
+      l += exp64<kBf16, kFp8>(sv, sl2x2, nmu2, pscale, pk);
+      store_p<kFp8>(tSc, pk);  // over S columns [0, 32) / [0, 16), already read
+      tmem_ld64(tSc + 64, sv);  // keys 64-127
+      if (flag) mask64(sv, am[2], am[3]);
+      l += exp64<kBf16, kFp8>(sv, sl2x2, nmu2, pscale, pk);
+      store_p<kFp8>(tSc + kPHalf, pk);
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&p_full[bb]);
+      mbar_arrive(&p_full[cls]);
     }
     // ---------------------------------------------------------- epilogue
+    // Merge the two classes: O = (a0 O0 + a1 O1) / (a0 l0 + a1 l1) with
+    // a_c = 2^(m_c - max(m0, m1)).  Each class writes half of the D columns.
     using Elem = typename std::conditional<kBf16, __nv_bfloat16, __half>::type;
     Elem* obase = nullptr;
     float* lse = nullptr;
@@ -504,38 +544,57 @@ __global__ void __launch_bounds__(kThreads, 1)
       obase = reinterpret_cast<Elem*>(prm.o) + b * prm.o_sb + static_cast<int64_t>(tok) * prm.o_st + h * prm.o_sh;
       if (prm.lse) lse = prm.lse + (static_cast<int64_t>(b) * prm.heads + h) * prm.n_video + tok;
     }
-    if (obase) obase += half * (D / 2);
-    if (ok && n > 0) {
-      const bool got = __all_sync(0xFFFFFFFFu, mbar_wait(&pv_done[(n - 1) & 1], ((n - 1) >> 1) & 1, abort,
-                                                        prm.err, LVSA_ERR_DEVICE_TIMEOUT));
-      float l_other;
-      if (xchg(n & 1, l, got && !fail, l_other)) {
-        const float lt = l + l_other;
+    if (obase) obase += cls * (D / 2);
+    if (n > 0) {
+      const bool got =
+          ok && __all_sync(0xFFFFFFFFu, mbar_wait(o_done, 0, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT));
+      // After o_done no MMA reads the query tile any more: reuse it.
+      float* red_m = reinterpret_cast<float*>(sQ);   // [2 classes][128 rows]
+      float* red_l = red_m + 2 * kBM;                // NaN marks a class that timed out
+      red_m[cls * kBM + r] = m;
+      red_l[cls * kBM + r] = got ? l : __int_as_float(0x7FC00000);
+      asm volatile("bar.sync %0, 64;" ::"r"(pair_bar) : "memory");
+      const float m_o = red_m[(cls ^ 1) * kBM + r], l_o = red_l[(cls ^ 1) * kBM + r];
+      if (__all_sync(0xFFFFFFFFu, got && !isnan(l_o))) {
         tc_fence_after();
+        const float mm = fmaxf(m, m_o);
+        const float a_me = (m == kNegInf) ? 0.f : ex2_approx(m - mm);
+        const float a_ot = (m_o == kNegInf) ? 0.f : ex2_approx(m_o - mm);
+        const float lt = l * a_me + l_o * a_ot;
         const float inv = (lt > 0.f) ? vref / lt : 0.f;
+        const float s0 = (cls == 0 ? a_me : a_ot) * inv, s1 = (cls == 1 ? a_me : a_ot) * inv;
+        const bool use1 = n > 1;  // O buffer 1 is written only when the list has two or more tiles
 #pragma unroll
         for (int c = 0; c < D / 64; ++c) {
-          uint32_t t[32];
-          tmem_ld32(tOr + c * 32, t);
+          const uint32_t col = cls * (D / 2) + c * 32;
+          uint32_t t0[32], t1[32];
+          tmem_ld32(tO + lane_base + col, t0);
+          if (use1) tmem_ld32(tO + 128 + lane_base + col, t1);
           if (valid && obase) {
             uint32_t pk[16];
 #pragma unroll
-            for (int i = 0; i < 16; ++i)
-              pk[i] = pack2(__uint_as_float(t[2 * i]) * inv, __uint_as_float(t[2 * i + 1]) * inv, kBf16);
+            for (int i = 0; i < 16; ++i) {
+              float x0 = __uint_as_float(t0[2 * i]) * s0, x1 = __uint_as_float(t0[2 * i + 1]) * s0;
+              if (use1) {
+                x0 = fmaf(__uint_as_float(t1[2 * i]), s1, x0);
+                x1 = fmaf(__uint_as_float(t1[2 * i + 1]), s1, x1);
+              }
+              pk[i] = pack2(x0, x1, kBf16);
+            }
             uint4* dst = reinterpret_cast<uint4*>(obase + c * 32);
 #pragma unroll
             for (int i = 0; i < 4; ++i) dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
           }
         }
-        if (valid && lse && half == 0) *lse = (lt > 0.f) ? (m + __log2f(lt)) * 0.69314718055994531f : kNegInf;
+        if (valid && lse && cls == 0) *lse = (lt > 0.f) ? (mm + __log2f(lt)) * 0.69314718055994531f : kNegInf;
       }
-    } else if (n == 0 && valid) {
+    } else if (valid) {
       if (obase) {
         uint4* dst = reinterpret_cast<uint4*>(obase);
 #pragma unroll
         for (int i = 0; i < D / 16; ++i) dst[i] = make_uint4(0u, 0u, 0u, 0u);
       }
-      if (lse && half == 0) *lse = kNegInf;
+      if (lse && cls == 0) *lse = kNegInf;
     }
   }
 
