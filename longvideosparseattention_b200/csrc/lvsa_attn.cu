@@ -198,12 +198,6 @@ __device__ __forceinline__ void mask64(uint32_t (&sv)[64], uint32_t w0, uint32_t
     if (!((((i < 32) ? w0 : w1) >> (i & 31)) & 1u)) sv[i] = __float_as_uint(kNegInf);
 }
 
-__device__ __forceinline__ void mask32(uint32_t (&sv)[32], uint32_t w) {
-#pragma unroll
-  for (int i = 0; i < 32; ++i)
-    if (!((w >> i) & 1u)) sv[i] = __float_as_uint(kNegInf);
-}
-
 __device__ __forceinline__ float max64(const uint32_t (&sv)[64]) {
   float mx[8];
 #pragma unroll
@@ -215,19 +209,6 @@ __device__ __forceinline__ float max64(const uint32_t (&sv)[64]) {
 #pragma unroll
   for (int i = 0; i < 8; ++i) mx[i] = fmaxf(mx[i], __uint_as_float(sv[56 + i]));
   return fmaxf(fmax3(mx[0], mx[1], mx[2]), fmax3(fmax3(mx[3], mx[4], mx[5]), mx[6], mx[7]));
-}
-
-__device__ __forceinline__ float max32(const uint32_t (&sv)[32]) {
-  float mx[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) mx[i] = fmax3(__uint_as_float(sv[i]), __uint_as_float(sv[4 + i]), __uint_as_float(sv[8 + i]));
-#pragma unroll
-  for (int k = 12; k < 28; k += 8)
-#pragma unroll
-    for (int i = 0; i < 4; ++i) mx[i] = fmax3(mx[i], __uint_as_float(sv[k + i]), __uint_as_float(sv[k + 4 + i]));
-#pragma unroll
-  for (int i = 0; i < 4; ++i) mx[i] = fmaxf(mx[i], __uint_as_float(sv[28 + i]));
-  return fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
 }
 
 // P = 2^(s * sl2 - mu) for 64 key columns, packed for the PV MMA: bf16/f16
@@ -482,16 +463,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_after();
       uint32_t sv[64];
-      tmem_ld64(tSc, sv);  // keys 0-63
       float mx_hi;
       {
-        uint32_t t[32];
-        tmem_ld32(tSc + 64, t);
-        if (flag) mask32(t, am[2]);
-        mx_hi = max32(t);
-        tmem_ld32(tSc + 96, t);
-        if (flag) mask32(t, am[3]);
-        mx_hi = fmaxf(mx_hi, max32(t));
+        uint32_t hv[64];
+        tmem_ld64x2(tSc, tSc + 64, sv, hv);  // keys 0-63 kept; keys 64-127 only for the max
+        if (flag) mask64(hv, am[2], am[3]);
+        mx_hi = max64(hv);
       }
       if (flag) mask64(sv, am[0], am[1]);
       const float m_new = fmaxf(m, fmaxf(max64(sv), mx_hi) * sl2);
