@@ -160,6 +160,45 @@ typedef struct LvsaFp8Scales {
  * `dtype` naming the OUTPUT type (bf16 or f16).  head_dim 128 only. */
 int lvsa_attn_fwd_fp8(const LvsaAttnArgs* args, const LvsaFp8Scales* scales, void* stream);
 
+/* ---- QK prologue: per-token norm + rotary embedding, fused, in place ----
+ * Replaces, for one of q or k, the two elementwise passes the adapters run
+ * before attention: the QK norm and the interleaved-pair RoPE
+ *   Wan:          norm_q/norm_k = RMSNorm over the H*D row
+ *                 (lvsa/adapters/wan.py:48-67) + apply_rotary_emb
+ *                 (lvsa/rope.py:10-28, lvsa/adapters/wan.py:103-119)
+ *   HunyuanVideo: RMSNorm per head (lvsa/adapters/hunyuan_video.py:71-103)
+ *                 + RoPE on video tokens (:156-205)
+ *   CogVideoX:    LayerNorm per head (lvsa/adapters/cogvideox.py:88-117)
+ *                 + RoPE on video tokens (:169-217)
+ * x [B, S, H, D] is read once and written once (fp32 arithmetic, one
+ * rounding to the storage type).  RoPE: pair (x0, x1) at dims (2p, 2p+1)
+ * becomes (x0 c - x1 s, x0 s + x1 c) with c = cos[t][p], s = sin[t][p] for
+ * token t = rope_offset + position in x; cos/sin are [*, S_table, D/2] fp32
+ * (the even entries of the reference's cos table and the odd entries of its
+ * sin table).  cos = NULL: norm only (text tokens). */
+enum { LVSA_DTYPE_F32 = 3 };
+enum {
+  LVSA_NORM_NONE = 0,
+  LVSA_NORM_RMS_ROW = 1,   /* RMS over all H*D values of a token; weight [H*D] */
+  LVSA_NORM_RMS_HEAD = 2,  /* RMS over each head's D values; weight [D]        */
+  LVSA_NORM_LAYER_HEAD = 3 /* LayerNorm over each head's D values; weight, bias [D] */
+};
+typedef struct LvsaQkPrologue {
+  LvsaTensor x;            /* in/out, stride 1 over D, 16-byte aligned rows     */
+  int32_t dtype;           /* LVSA_DTYPE_BF16 / _F16                            */
+  int32_t batch, seq, heads, head_dim; /* head_dim 64 or 128; H*D <= 8192       */
+  int32_t norm;            /* LVSA_NORM_*                                       */
+  int32_t weight_dtype;    /* LVSA_DTYPE_BF16 / _F16 / _F32 (weight and bias)   */
+  const void* weight;      /* NULL: no scale                                    */
+  const void* bias;        /* LayerNorm only; NULL: no shift                    */
+  float eps;
+  const float* cos;        /* NULL: no rotary embedding                         */
+  const float* sin;
+  int64_t rope_stride_b;   /* elements between batches of the tables; 0: shared */
+  int32_t rope_offset;     /* table row of x's first token (sequence shards)    */
+} LvsaQkPrologue;
+int lvsa_qk_prologue(const LvsaQkPrologue* args, void* stream);
+
 /* FP8 attention that allocates no device memory.  No counterpart in the
  * reference: an addition of this library.
  *

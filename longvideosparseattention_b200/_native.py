@@ -27,9 +27,11 @@ LVSA_DTYPE_F16 = 1
 LVSA_MAX_FRAMES = 2048
 
 EXPORTED_SYMBOLS = ("lvsa_mask_layout", "lvsa_build_mask", "lvsa_attn_fwd", "lvsa_quantize_e4m3",
-                    "lvsa_attn_fwd_fp8", "lvsa_attn_fwd_fp8_noalloc", "lvsa_status_str",
+                    "lvsa_attn_fwd_fp8", "lvsa_attn_fwd_fp8_noalloc", "lvsa_qk_prologue", "lvsa_status_str",
                     "lvsa_abi_version")
 LVSA_DTYPE_E4M3 = 2
+LVSA_DTYPE_F32 = 3
+LVSA_NORM_NONE, LVSA_NORM_RMS_ROW, LVSA_NORM_RMS_HEAD, LVSA_NORM_LAYER_HEAD = 0, 1, 2, 3
 
 _i32, _i64, _vp = ctypes.c_int32, ctypes.c_int64, ctypes.c_void_p
 
@@ -68,6 +70,13 @@ class LvsaAttnArgs(ctypes.Structure):
                 ("n_q_tiles", _i32), ("n_k_video_tiles", _i32),
                 ("frame_bits", _vp), ("tile_indptr", _vp), ("tile_indices", _vp),
                 ("tile_flags", _vp), ("error_word", _vp)]
+
+
+class LvsaQkPrologue(ctypes.Structure):
+    _fields_ = [("x", LvsaTensor), ("dtype", _i32), ("batch", _i32), ("seq", _i32), ("heads", _i32),
+                ("head_dim", _i32), ("norm", _i32), ("weight_dtype", _i32), ("weight", _vp), ("bias", _vp),
+                ("eps", ctypes.c_float), ("cos", _vp), ("sin", _vp), ("rope_stride_b", _i64),
+                ("rope_offset", _i32)]
 
 
 class LvsaFp8Scales(ctypes.Structure):
@@ -109,6 +118,8 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
         lib.lvsa_attn_fwd_fp8.restype = ctypes.c_int
         lib.lvsa_attn_fwd_fp8_noalloc.argtypes = [ctypes.POINTER(LvsaAttnArgs), _vp]
         lib.lvsa_attn_fwd_fp8_noalloc.restype = ctypes.c_int
+        lib.lvsa_qk_prologue.argtypes = [ctypes.POINTER(LvsaQkPrologue), _vp]
+        lib.lvsa_qk_prologue.restype = ctypes.c_int
         lib.lvsa_status_str.argtypes = [ctypes.c_int]
         lib.lvsa_status_str.restype = ctypes.c_char_p
         lib.lvsa_abi_version.argtypes = []

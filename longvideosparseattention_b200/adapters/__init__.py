@@ -7,6 +7,8 @@ from .base import ModelAdapter
 
 _ADAPTER_REGISTRY: Dict[str, Tuple[str, str]] = {
     "wan": ("longvideosparseattention_b200.adapters.wan", "WanAdapter"),
+    "hunyuan_video": ("longvideosparseattention_b200.adapters.hunyuan_video", "HunyuanVideoAdapter"),
+    "cogvideox": ("longvideosparseattention_b200.adapters.cogvideox", "CogVideoXAdapter"),
 }
 
 

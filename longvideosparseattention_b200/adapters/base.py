@@ -52,6 +52,17 @@ class ModelAdapter(ABC):
                      ) -> Tuple[torch.Tensor, torch.Tensor]:
         """RoPE on video Q and K (sliced to this rank's tokens)."""
 
+    def project_qkv(self, attn: Any, hidden_states: torch.Tensor,
+                    encoder_hidden_states: Optional[torch.Tensor], rotary_emb: Any,
+                    local_seq: int, rank: int, world: int
+                    ) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+        """Video Q, K, V ready for attention: what ``extract_qkv`` followed by
+        ``apply_rotary`` returns.  Adapters whose QK norm and rotation the
+        fused prologue kernel covers override this to run both in one pass."""
+        q, k, v = self.extract_qkv(attn, hidden_states, encoder_hidden_states)
+        q, k = self.apply_rotary(q, k, rotary_emb, local_seq, rank, world)
+        return q, k, v
+
     @abstractmethod
     def output_projection(self, attn: Any, hidden_states: torch.Tensor,
                           query_dtype: torch.dtype) -> torch.Tensor:

@@ -41,6 +41,10 @@ def slice_rotary(rotary_emb: Sequence[torch.Tensor], local_seq: int, rank: int, 
 
 
 class WanAdapter(ModelAdapter):
+    def __init__(self) -> None:
+        from ..prologue import RopeTableCache
+        self._rope_cache = RopeTableCache()
+
     def patches_per_frame(self, height: int, width: int, pipe: Any) -> int:
         ps = getattr(pipe.transformer.config, "patch_size", [1, 2, 2])
         ps = int(ps[1]) if isinstance(ps, (list, tuple)) else int(ps)
@@ -78,6 +82,32 @@ class WanAdapter(ModelAdapter):
         k = attn.norm_added_k(attn.add_k_proj(encoder_hidden_states))
         v = attn.add_v_proj(encoder_hidden_states)
         return self._heads(attn, k), self._heads(attn, v)
+
+    def project_qkv(self, attn, hidden_states, encoder_hidden_states, rotary_emb, local_seq, rank, world):
+        """Projections, then the RMSNorm over the H*D row and the rotation of
+        q and k in one pass each (the fused prologue kernel) when it applies;
+        otherwise ``extract_qkv`` + ``apply_rotary``."""
+        from ..prologue import fused_prologue_ok, norm_spec, qk_norm_rope
+        if not hidden_states.is_cuda:
+            return super().project_qkv(attn, hidden_states, encoder_hidden_states, rotary_emb, local_seq, rank, world)
+        if getattr(attn, "fused_projections", False) and hasattr(attn, "to_qkv"):
+            q, k, v = attn.to_qkv(hidden_states).chunk(3, dim=-1)
+        else:
+            q, k, v = attn.to_q(hidden_states), attn.to_k(hidden_states), attn.to_v(hidden_states)
+        q, k, v = self._heads(attn, q), self._heads(attn, k), self._heads(attn, v)
+        dim = q.shape[-2] * q.shape[-1]
+        sq = norm_spec(getattr(attn, "norm_q", None), False, dim, q.dtype)
+        sk = norm_spec(getattr(attn, "norm_k", None), False, dim, k.dtype)
+        tabs = None if rotary_emb is None else self._rope_cache.get(rotary_emb, local_seq, rank, world)
+        if sq is not None and sk is not None and (rotary_emb is None or tabs is not None) and fused_prologue_ok(q, k):
+            cs, sn, off = tabs if tabs is not None else (None, None, 0)
+            qk_norm_rope(q, *sq, cos=cs, sin=sn, rope_offset=off)
+            qk_norm_rope(k, *sk, cos=cs, sin=sn, rope_offset=off)
+            return q, k, v
+        q = self._heads(attn, attn.norm_q(q.flatten(2, 3)))
+        k = self._heads(attn, attn.norm_k(k.flatten(2, 3)))
+        q, k = self.apply_rotary(q, k, rotary_emb, local_seq, rank, world)
+        return q, k, v
 
     def apply_rotary(self, query, key, rotary_emb, local_seq, rank, world):
         if rotary_emb is None:

@@ -176,7 +176,11 @@ class DistributedLVSAProcessor:
         encoder_img = None
         if encoder_hidden_states is not None:
             encoder_hidden_states, encoder_img = adapter.split_encoder_for_cross_attn(attn, encoder_hidden_states)
-        query, key, value = adapter.extract_qkv(attn, hidden_states, encoder_hidden_states)
+        local_seq = hidden_states.shape[1]
+        # Projections, QK norm and rotary embedding (fused into one pass per
+        # tensor by the adapter where the prologue kernel applies).
+        query, key, value = adapter.project_qkv(attn, hidden_states, encoder_hidden_states, rotary_emb,
+                                                local_seq, self.rank, self.world)
         query_dtype = query.dtype
         enc_q = enc_k = enc_v = None
         enc_len = 0
@@ -185,8 +189,6 @@ class DistributedLVSAProcessor:
             if enc is not None:
                 enc_q, enc_k, enc_v = enc
                 enc_len = enc_q.shape[1]
-        local_seq = hidden_states.shape[1]
-        query, key = adapter.apply_rotary(query, key, rotary_emb, local_seq, self.rank, self.world)
 
         enc_out = None
         if self._geometry_matches(local_seq):

@@ -369,3 +369,45 @@ def attention_torch_cpu(q, k, v, pattern: Dict, text_k=None, text_v=None,
                                            vc.transpose(1, 2), enable_gqa=gqa)
         out[:, f * P:(f + 1) * P] = o.transpose(1, 2)
     return out
+
+
+# ---------------------------------------------------------------------------
+# QK prologue (the adapters' norm + rotary embedding), fp32, torch on CPU.
+def norm_rope(x, norm, weight=None, bias=None, eps=1e-6, cos=None, sin=None, rope_offset=0):
+    """x [B, S, H, D] -> fp32.  norm: None | "rms_row" (RMSNorm over the H*D
+    row, Wan's norm_q/norm_k, lvsa/adapters/wan.py:48-67) | "rms_head"
+    (per-head RMSNorm, lvsa/adapters/hunyuan_video.py:71-103) | "layer_head"
+    (per-head LayerNorm, lvsa/adapters/cogvideox.py:88-117); then the
+    interleaved-pair rotation of lvsa/rope.py:10-28 with cos/sin given as pair
+    angle tables [S_tab, D/2] or [B, S_tab, D/2], rows rope_offset + s."""
+    import torch
+    B, S, H, D = x.shape
+    f = x.float()
+    if norm == "rms_row":
+        r = f.reshape(B, S, H * D)
+        r = r * torch.rsqrt(r.pow(2).mean(-1, keepdim=True) + eps)
+        if weight is not None:
+            r = r * weight.float()
+        f = r.reshape(B, S, H, D)
+    elif norm == "rms_head":
+        f = f * torch.rsqrt(f.pow(2).mean(-1, keepdim=True) + eps)
+        if weight is not None:
+            f = f * weight.float()
+    elif norm == "layer_head":
+        mu = f.mean(-1, keepdim=True)
+        f = (f - mu) * torch.rsqrt((f - mu).pow(2).mean(-1, keepdim=True) + eps)
+        if weight is not None:
+            f = f * weight.float()
+        if bias is not None:
+            f = f + bias.float()
+    if cos is not None:
+        c = cos.float()[..., rope_offset:rope_offset + S, :]
+        s = sin.float()[..., rope_offset:rope_offset + S, :]
+        c = c.unsqueeze(-2) if c.dim() == 3 else c[None, :, None, :]
+        s = s.unsqueeze(-2) if s.dim() == 3 else s[None, :, None, :]
+        x0, x1 = f[..., 0::2], f[..., 1::2]
+        out = torch.empty_like(f)
+        out[..., 0::2] = x0 * c - x1 * s
+        out[..., 1::2] = x0 * s + x1 * c
+        f = out
+    return f

@@ -4,9 +4,12 @@ Run in a container where the reference checkout exists:
 
     python tests/golden/make_golden.py /path/to/LongVideoSparseAttention
 
-It writes ``patterns.npz`` (frame-level ``LVSAMetadata.build`` outputs) and
+It writes ``patterns.npz`` (frame-level ``LVSAMetadata.build`` outputs),
 ``attn_*.npz`` (seeded bf16-representable inputs with the reference's fp32
-``lvsa_sdpa`` output and dense text-query rows).  The fixtures are committed;
+``lvsa_sdpa`` output and dense text-query rows) and ``rope.npz`` (the
+reference's ``apply_rotary_emb`` / ``slice_rotary_emb`` on seeded inputs)
+and ``adapters.npz`` (the reference HunyuanVideo / CogVideoX adapters on
+seeded mock modules); ``--only rope|adapters`` writes just one of them.  The fixtures are committed;
 the tests never need the reference at run time.
 """
 
@@ -125,5 +128,91 @@ def main(ref_root: str) -> None:
         print("wrote", name)
 
 
+def rope_golden(ref_root: str) -> None:
+    """lvsa/rope.py:10-28 (apply_rotary_emb) and :31-57 (slice_rotary_emb)."""
+    sys.path.insert(0, ref_root)
+    from lvsa.rope import apply_rotary_emb, slice_rotary_emb
+    g = torch.Generator().manual_seed(4242)
+    arrays = {}
+    for name, (S, H, D) in {"d128": (24, 3, 128), "d64": (17, 2, 64)}.items():
+        x = bf16_round(torch.randn(1, S, H, D, generator=g))
+        ang = torch.rand(S, D // 2, generator=g) * 6.0
+        # Wan layout [1, S, 1, D]: each pair angle repeated in the even and odd slot.
+        cos = torch.cos(ang).repeat_interleave(2, -1)[None, :, None, :]
+        sin = torch.sin(ang).repeat_interleave(2, -1)[None, :, None, :]
+        arrays[f"{name}.x"] = x.numpy()
+        arrays[f"{name}.cos"] = cos.numpy()
+        arrays[f"{name}.sin"] = sin.numpy()
+        arrays[f"{name}.out"] = apply_rotary_emb(x, cos, sin).numpy()
+        c1, s1 = slice_rotary_emb((cos, sin), S // 3, 1, 3)
+        arrays[f"{name}.slice_cos"] = c1.numpy()
+        arrays[f"{name}.slice_sin"] = s1.numpy()
+    np.savez_compressed(os.path.join(HERE, "rope.npz"), **arrays)
+    print("wrote rope")
+
+
+def adapters_golden(ref_root: str) -> None:
+    """The reference HunyuanVideo / CogVideoX adapters (lvsa/adapters/
+    hunyuan_video.py, cogvideox.py) on seeded mock modules: extract_qkv,
+    extract_encoder_qkv, apply_rotary (its RoPE fallback, lvsa/rope.py),
+    output_projection and format_output."""
+    import importlib.util
+    sys.path.insert(0, ref_root)
+    from lvsa.adapters import get_adapter
+    spec = importlib.util.spec_from_file_location("adapter_mocks", os.path.join(os.path.dirname(HERE),
+                                                                                "adapter_mocks.py"))
+    mocks = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mocks)
+    MockAttn, rope_pair = mocks.MockAttn, mocks.rope_pair
+    arrays = {}
+    for name, norm, dual in (("hunyuan_video", "rms", True), ("cogvideox", "ln", False)):
+        dim, heads, S, St = 256, 4, 24, 7
+        attn = MockAttn(dim, heads, norm, dual, seed=len(name))
+        g = torch.Generator().manual_seed(99 + len(name))
+        hs = torch.randn(1, S, dim, generator=g)
+        ehs = torch.randn(1, St, dim, generator=g)
+        cos, sin = rope_pair(S, dim // heads, seed=5)
+        ad = get_adapter(name)
+        with torch.no_grad():
+            q, k, v = ad.extract_qkv(attn, hs, ehs)
+            q2, k2 = ad.apply_rotary(q, k, (cos, sin), S, 0, 1)
+            eq, ek, ev = ad.extract_encoder_qkv(attn, ehs)
+            o = torch.randn(1, S, heads, dim // heads, generator=g)
+            eo = torch.randn(1, St, heads, dim // heads, generator=g)
+            hp = ad.output_projection(attn, o, torch.float32)
+            fo = ad.format_output(attn, hp, eo, St, torch.float32)
+        for key, t in dict(hs=hs, ehs=ehs, cos=cos, sin=sin, q=q2, k=k2, v=v, eq=eq, ek=ek, ev=ev,
+                           o=o, eo=eo, out_video=fo[0], out_text=fo[1]).items():
+            arrays[f"{name}.{key}"] = t.numpy()
+        arrays[f"{name}.ppf"] = np.asarray([ad.patches_per_frame(480, 832, _Pipe(name)),
+                                            ad.latent_frames(121, _Pipe(name)),
+                                            ad.reference_latent_frames(_Pipe(name))])
+    np.savez_compressed(os.path.join(HERE, "adapters.npz"), **arrays)
+    print("wrote adapters")
+
+
+class _Pipe:
+    """Minimal pipeline stand-in for the geometry helpers."""
+
+    def __init__(self, name: str):
+        class _Cfg:
+            patch_size = 2 if name != "hunyuan_video" else [1, 1, 1]
+            patch_size_t = None
+
+        class _Tr:
+            config = _Cfg()
+        self.transformer = _Tr()
+        self.vae_scale_factor_spatial = 16 if name == "hunyuan_video" else 8
+        self.vae_scale_factor_temporal = 4
+
+
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else os.environ.get("LVSA_REFERENCE_ROOT", "."))
+    args = [a for a in sys.argv[1:] if not a.startswith("--")]
+    root = args[0] if args else os.environ.get("LVSA_REFERENCE_ROOT", ".")
+    if "--only" in sys.argv:
+        which = sys.argv[sys.argv.index("--only") + 1]
+        {"rope": rope_golden, "adapters": adapters_golden}[which](root)
+    else:
+        main(root)
+        rope_golden(root)
+        adapters_golden(root)
