@@ -408,6 +408,80 @@ def run_reference(args, cfg):
     print(json.dumps(line), flush=True)
 
 
+def run_prologue(args, cfg):
+    """--prologue: the fused QK prologue (norm + rotary, one pass per tensor)
+    on q and k of the configuration's shape, against the unfused torch path
+    the adapters run otherwise (module norm, then the rotation).  HBM-bound:
+    algorithmic bytes = read + write of q and k, plus the rotary tables."""
+    import torch
+    from longvideosparseattention_b200.prologue import qk_norm_rope
+    dev = torch.device("cuda", 0)
+    S, H, D = cfg["T"] * cfg["P"], cfg["H"], cfg["D"]
+    per_head = args.config != "cfg2" and args.config != "cfg3"
+    norm = ("layer_head" if args.config == "cfg5" else "rms_head") if per_head else "rms_row"
+    g = torch.Generator(device=dev).manual_seed(7)
+    xs = [torch.randn(1, S, H, D, device=dev, generator=g).bfloat16() for _ in range(2)]
+    w = (1 + 0.1 * torch.randn(D if per_head else H * D, device=dev, generator=g)).bfloat16()
+    b = torch.zeros(D, device=dev, dtype=torch.bfloat16) if norm == "layer_head" else None
+    ang = torch.rand(S, D // 2, device=dev, generator=g) * 6.0
+    cs, sn = torch.cos(ang), torch.sin(ang)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # 256 MB > L2 between steps
+
+    def fused():
+        for x in xs:
+            qk_norm_rope(x, norm, w, b, 1e-6, cs, sn)
+
+    cos_full, sin_full = cs.repeat_interleave(2, -1)[None, :, None, :], sn.repeat_interleave(2, -1)[None, :, None, :]
+
+    def unfused():
+        for x in xs:
+            if norm == "rms_row":
+                y = torch.nn.functional.rms_norm(x.flatten(2), (H * D,), w, 1e-6).unflatten(2, (H, D))
+            elif norm == "rms_head":
+                y = torch.nn.functional.rms_norm(x, (D,), w, 1e-6)
+            else:
+                y = torch.nn.functional.layer_norm(x, (D,), w, b, 1e-6)
+            x1, x2 = y.unflatten(-1, (-1, 2)).unbind(-1)
+            out = torch.empty_like(y)
+            out[..., 0::2] = x1 * cos_full[..., 0::2] - x2 * sin_full[..., 1::2]
+            out[..., 1::2] = x1 * sin_full[..., 1::2] + x2 * cos_full[..., 0::2]
+            x.copy_(out)
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        times = []
+        for _ in range(args.steps):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize()
+            times.append(e0.elapsed_time(e1))
+        return sorted(times)[len(times) // 2]
+
+    with ClockSampler(0) as sampler:
+        ms = timed(fused)
+    clocks = sampler.summary()
+    ms_unfused = timed(unfused)
+    nbytes = 2 * (2 * S * H * D * 2) + 2 * S * (D // 2) * 4 * 2  # q, k read + write; cos/sin per tensor
+    pk, src = peaks()
+    gbs = nbytes / ms / 1e6
+    print(json.dumps({
+        "metric": "qk-prologue (norm + RoPE of q and k) GB/s", "value": round(gbs, 1), "unit": "GB/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"{args.config} q,k prologue", "tokens": S, "heads": H, "head_dim": D,
+                   "norm": norm, "l2": "256 MB written between steps (flush)"},
+        "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(gbs / pk["hbm_gbs"], 4), "traffic": None, "algorithmic_bytes": nbytes,
+                     "peak_source": f"{src} hbm_gbs"},
+        "unfused_torch_ms": round(ms_unfused, 4), "speedup_vs_unfused": round(ms_unfused / ms, 2),
+        "clocks": clocks, "gpu_launches": 2 * args.steps}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -424,6 +498,8 @@ def main():
                          "parallelism over one set of layers (strong scaling)")
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--prologue", action="store_true",
+                    help="time the fused QK prologue (norm + RoPE) instead of the attention step")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     cfg = dict(CONFIGS[args.config])
@@ -431,7 +507,9 @@ def main():
         cfg["layers"] = args.layers
     if int(os.environ.get("WORLD_SIZE", "1")) > 1 or args.gpus > 1:
         args.cpu_baseline = False
-    if args.impl == "reference":
+    if args.prologue:
+        run_prologue(args, cfg)
+    elif args.impl == "reference":
         run_reference(args, cfg)
     else:
         run_b200(args, cfg)

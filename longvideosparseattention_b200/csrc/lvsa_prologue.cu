@@ -47,111 +47,167 @@ __device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
   return u;
 }
 
-// 8 consecutive parameters (weight or bias) starting at element i, as fp32.
-__device__ __forceinline__ void load_param8(const void* p, int dt, int64_t i, float (&f)[8]) {
-  if (dt == LVSA_DTYPE_F32) {
-    const float4 a = reinterpret_cast<const float4*>(static_cast<const float*>(p) + i)[0];
-    const float4 b = reinterpret_cast<const float4*>(static_cast<const float*>(p) + i)[1];
-    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
-  } else if (dt == LVSA_DTYPE_BF16) {
-    unpack8<__nv_bfloat16>(*reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p) + i), f);
-  } else {
-    unpack8<__half>(*reinterpret_cast<const uint4*>(static_cast<const __half*>(p) + i), f);
-  }
-}
-
 // Sum over aligned groups of `group` lanes (a power of two <= 32).
 __device__ __forceinline__ float group_sum(float v, int group) {
   for (int o = group >> 1; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
   return v;
 }
 
-// Norm + rotary embedding of one 16-byte vector (8 values at dims d0..d0+7).
-template <typename T>
-__device__ __forceinline__ uint4 finish8(const LvsaQkPrologue& a, const uint4& u, float mean, float rstd,
-                                         int64_t w_idx, int d0, const float* cs, const float* sn) {
-  float f[8];
-  unpack8<T>(u, f);
-  if (a.norm != LVSA_NORM_NONE) {
-    float w[8] = {1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f}, bb[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    if (a.weight) load_param8(a.weight, a.weight_dtype, w_idx, w);
-    if (a.bias && a.norm == LVSA_NORM_LAYER_HEAD) load_param8(a.bias, a.weight_dtype, d0, bb);
-#pragma unroll
-    for (int k = 0; k < 8; ++k) f[k] = (f[k] - mean) * rstd * w[k] + bb[k];
+// Eight norm parameters in their storage type: one 16-byte load for bf16 /
+// f16, two for fp32.
+template <typename WT>
+struct WPack {
+  uint4 u;
+  __device__ __forceinline__ void load(const void* p, int64_t i) {
+    u = __ldg(reinterpret_cast<const uint4*>(static_cast<const WT*>(p) + i));
   }
-  if (cs) {
-    const float4 c = *reinterpret_cast<const float4*>(cs + d0 / 2);
-    const float4 s = *reinterpret_cast<const float4*>(sn + d0 / 2);
-    const float cc[4] = {c.x, c.y, c.z, c.w}, ss[4] = {s.x, s.y, s.z, s.w};
-#pragma unroll
-    for (int p = 0; p < 4; ++p) {
-      const float x0 = f[2 * p], x1 = f[2 * p + 1];
-      f[2 * p] = x0 * cc[p] - x1 * ss[p];
-      f[2 * p + 1] = x0 * ss[p] + x1 * cc[p];
-    }
+  __device__ __forceinline__ void get(float (&f)[8]) const { unpack8<WT>(u, f); }
+};
+template <>
+struct WPack<float> {
+  float4 a, b;
+  __device__ __forceinline__ void load(const void* p, int64_t i) {
+    a = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(p) + i));
+    b = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(p) + i) + 1);
   }
-  return pack8<T>(f);
+  __device__ __forceinline__ void get(float (&f)[8]) const {
+    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+  }
+};
+
+// Rotation of the 4 pairs of a vector by the angles (c, s).
+__device__ __forceinline__ void rotate8(float (&f)[8], const float4& c, const float4& s) {
+  const float cc[4] = {c.x, c.y, c.z, c.w}, ss[4] = {s.x, s.y, s.z, s.w};
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const float x0 = f[2 * q], x1 = f[2 * q + 1];
+    f[2 * q] = x0 * cc[q] - x1 * ss[q];
+    f[2 * q + 1] = x0 * ss[q] + x1 * cc[q];
+  }
 }
 
-// VPL: vectors per lane (the row holds at most 32 VPL vectors).  kKeep: the
-// row norm keeps the row in registers between its two passes; otherwise the
-// second pass reads it again (an L1 hit).
-template <typename T, int VPL, bool kKeep>
-__global__ void __launch_bounds__(32 * kWarpsPerBlock)
-    qk_prologue_kernel(const LvsaQkPrologue a, int64_t rows) {
+// With D/8 lanes per head (a power of two <= 32), vector v = lane + 32 i
+// always covers dims d0 = (lane % (D/8)) * 8 .. +7 of its head: the rotation
+// angles and per-head norm parameters are one load per lane and row.
+struct LaneRow {
+  int bi, t, d0;
+  bool rope;
+  float4 c, s;
+};
+
+__device__ __forceinline__ LaneRow lane_row(const LvsaQkPrologue& a, int64_t row, int lane) {
+  LaneRow r;
+  r.bi = static_cast<int>(row / a.seq);
+  r.t = static_cast<int>(row % a.seq);
+  r.d0 = (lane % (a.head_dim / 8)) * 8;
+  r.rope = a.cos != nullptr;
+  r.c = r.s = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (r.rope) {
+    const int64_t off = r.bi * a.rope_stride_b + static_cast<int64_t>(a.rope_offset + r.t) * (a.head_dim / 2) + r.d0 / 2;
+    r.c = __ldg(reinterpret_cast<const float4*>(a.cos + off));
+    r.s = __ldg(reinterpret_cast<const float4*>(a.sin + off));
+  }
+  return r;
+}
+
+// Row norm: one warp per token row (the statistic spans the row); all of the
+// row's vectors are loaded before any arithmetic.  kKeep: the row stays in
+// registers; otherwise the output pass reads it again (L1 hit).  The weights
+// are read in the output pass (L1 hits after the first rows), which keeps the
+// kernel at <= 85 registers, 3 blocks per SM: enough rows in flight to cover
+// HBM latency (keeping them as well halved the bandwidth).
+template <typename T, typename WT, int VPL, bool kKeep>
+__global__ void __launch_bounds__(32 * kWarpsPerBlock, 3)
+    qk_prologue_row_kernel(const LvsaQkPrologue a, int64_t rows) {
   const int lane = threadIdx.x & 31;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5);
   if (row >= rows) return;  // whole warp
-  const int bi = static_cast<int>(row / a.seq), t = static_cast<int>(row % a.seq);
-  const int D = a.head_dim, G = D / 8;  // vectors per head (a power of two <= 32)
-  const int nv = a.heads * G;           // vectors per row
-  T* base = static_cast<T*>(a.x.ptr) + bi * a.x.stride_b + static_cast<int64_t>(t) * a.x.stride_t;
-  auto vaddr = [&](int v) { return base + (v / G) * a.x.stride_h + (v % G) * 8; };
-  const float* cs = nullptr;
-  const float* sn = nullptr;
-  if (a.cos) {
-    const int64_t off = bi * a.rope_stride_b + static_cast<int64_t>(a.rope_offset + t) * (D / 2);
-    cs = a.cos + off;
-    sn = a.sin + off;
-  }
-
-  if (a.norm == LVSA_NORM_RMS_ROW) {
-    uint4 raw[kKeep ? VPL : 1];
-    float sq = 0.f;
-#pragma unroll
-    for (int i = 0; i < VPL; ++i) {
-      const int v = lane + 32 * i;
-      uint4 u = make_uint4(0u, 0u, 0u, 0u);
-      if (v < nv) u = *reinterpret_cast<const uint4*>(vaddr(v));
-      if constexpr (kKeep) raw[i] = u;
-      float f[8];
-      unpack8<T>(u, f);
-#pragma unroll
-      for (int k = 0; k < 8; ++k) sq += f[k] * f[k];
-    }
-    const float rstd = rsqrtf(group_sum(sq, 32) / (a.heads * D) + a.eps);
-#pragma unroll
-    for (int i = 0; i < VPL; ++i) {
-      const int v = lane + 32 * i;
-      if (v >= nv) continue;
-      uint4 u;
-      if constexpr (kKeep) u = raw[i];
-      else u = *reinterpret_cast<const uint4*>(vaddr(v));
-      *reinterpret_cast<uint4*>(vaddr(v)) = finish8<T>(a, u, 0.f, rstd, int64_t(v) * 8, (v % G) * 8, cs, sn);
-    }
-    return;
-  }
-  // Per-head norms (or none): the G vectors of a head are G consecutive lanes
-  // of one iteration, so each iteration is self-contained.
+  const LaneRow lr = lane_row(a, row, lane);
+  const int G = a.head_dim / 8, nv = a.heads * G;
+  T* base = static_cast<T*>(a.x.ptr) + lr.bi * a.x.stride_b + static_cast<int64_t>(lr.t) * a.x.stride_t;
+  auto vaddr = [&](int v) { return base + (v / G) * a.x.stride_h + lr.d0; };
+  uint4 raw[kKeep ? VPL : 1];
+  float sq = 0.f;
 #pragma unroll
   for (int i = 0; i < VPL; ++i) {
     const int v = lane + 32 * i;
     uint4 u = make_uint4(0u, 0u, 0u, 0u);
-    if (v < nv) u = *reinterpret_cast<const uint4*>(vaddr(v));
-    float mean = 0.f, rstd = 1.f;
+    if (v < nv) {
+      u = *reinterpret_cast<const uint4*>(vaddr(v));
+
+    }
+    if constexpr (kKeep) raw[i] = u;
+    float f[8];
+    unpack8<T>(u, f);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) sq += f[k] * f[k];
+  }
+  const float rstd = rsqrtf(group_sum(sq, 32) / (a.heads * a.head_dim) + a.eps);
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int v = lane + 32 * i;
+    if (v >= nv) continue;
+    float f[8], w[8] = {1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f};
+    if constexpr (kKeep) {
+      unpack8<T>(raw[i], f);
+      if (a.weight) {
+        WPack<WT> p;
+        p.load(a.weight, int64_t(v) * 8);
+        p.get(w);
+      }
+    } else {
+      unpack8<T>(*reinterpret_cast<const uint4*>(vaddr(v)), f);
+      if (a.weight) {
+        WPack<WT> p;
+        p.load(a.weight, int64_t(v) * 8);
+        p.get(w);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) f[k] = f[k] * rstd * w[k];
+    if (lr.rope) rotate8(f, lr.c, lr.s);
+    *reinterpret_cast<uint4*>(vaddr(v)) = pack8<T>(f);
+  }
+}
+
+// Per-head norm (or none): the G = D/8 vectors of a head are G consecutive
+// lanes of one 32-vector slice, so a warp takes VPL slices of a row
+// (blockIdx.y picks which) and needs no row-wide reduction.
+template <typename T, typename WT, int VPL>
+__global__ void __launch_bounds__(32 * kWarpsPerBlock)
+    qk_prologue_head_kernel(const LvsaQkPrologue a, int64_t rows) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5);
+  if (row >= rows) return;  // whole warp
+  const LaneRow lr = lane_row(a, row, lane);
+  const int D = a.head_dim, G = D / 8, nv = a.heads * G;
+  const int v0 = blockIdx.y * 32 * VPL;
+  T* base = static_cast<T*>(a.x.ptr) + lr.bi * a.x.stride_b + static_cast<int64_t>(lr.t) * a.x.stride_t;
+  auto vaddr = [&](int v) { return base + (v / G) * a.x.stride_h + lr.d0; };
+  uint4 raw[VPL];
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int v = v0 + lane + 32 * i;
+    raw[i] = v < nv ? *reinterpret_cast<const uint4*>(vaddr(v)) : make_uint4(0u, 0u, 0u, 0u);
+  }
+  float w[8] = {1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f}, bb[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  if (a.norm != LVSA_NORM_NONE && a.weight) {
+    WPack<WT> p;
+    p.load(a.weight, lr.d0);
+    p.get(w);
+  }
+  if (a.norm == LVSA_NORM_LAYER_HEAD && a.bias) {
+    WPack<WT> p;
+    p.load(a.bias, lr.d0);
+    p.get(bb);
+  }
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int v = v0 + lane + 32 * i;
+    float f[8];
+    unpack8<T>(raw[i], f);
     if (a.norm != LVSA_NORM_NONE) {
-      float f[8];
-      unpack8<T>(u, f);
+      float mean = 0.f;
       if (a.norm == LVSA_NORM_LAYER_HEAD) {
         float sum = 0.f;
 #pragma unroll
@@ -161,24 +217,42 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock)
       float q = 0.f;
 #pragma unroll
       for (int k = 0; k < 8; ++k) q += (f[k] - mean) * (f[k] - mean);
-      rstd = rsqrtf(group_sum(q, G) / D + a.eps);
+      const float rstd = rsqrtf(group_sum(q, G) / D + a.eps);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) f[k] = (f[k] - mean) * rstd * w[k] + bb[k];
     }
-    if (v < nv) *reinterpret_cast<uint4*>(vaddr(v)) = finish8<T>(a, u, mean, rstd, (v % G) * 8, (v % G) * 8, cs, sn);
+    if (lr.rope) rotate8(f, lr.c, lr.s);
+    if (v < nv) *reinterpret_cast<uint4*>(vaddr(v)) = pack8<T>(f);
   }
+}
+
+template <typename T, typename WT>
+int launch_prologue_t(const LvsaQkPrologue* a, cudaStream_t s) {
+  const int64_t rows = static_cast<int64_t>(a->batch) * a->seq;
+  const int nv = a->heads * (a->head_dim / 8);
+  const unsigned gx = static_cast<unsigned>((rows + kWarpsPerBlock - 1) / kWarpsPerBlock);
+  const dim3 block(32 * kWarpsPerBlock);
+  if (a->norm == LVSA_NORM_RMS_ROW) {
+    const dim3 grid(gx);
+    if (nv <= 32) qk_prologue_row_kernel<T, WT, 1, true><<<grid, block, 0, s>>>(*a, rows);
+    else if (nv <= 64) qk_prologue_row_kernel<T, WT, 2, true><<<grid, block, 0, s>>>(*a, rows);
+    else if (nv <= 128) qk_prologue_row_kernel<T, WT, 4, true><<<grid, block, 0, s>>>(*a, rows);
+    else if (nv <= 256) qk_prologue_row_kernel<T, WT, 8, true><<<grid, block, 0, s>>>(*a, rows);
+    else if (nv <= 512) qk_prologue_row_kernel<T, WT, 16, false><<<grid, block, 0, s>>>(*a, rows);
+    else qk_prologue_row_kernel<T, WT, 32, false><<<grid, block, 0, s>>>(*a, rows);
+  } else if (nv <= 32) {
+    qk_prologue_head_kernel<T, WT, 1><<<dim3(gx, 1), block, 0, s>>>(*a, rows);
+  } else {
+    qk_prologue_head_kernel<T, WT, 4><<<dim3(gx, (nv + 127) / 128), block, 0, s>>>(*a, rows);
+  }
+  return cudaGetLastError() == cudaSuccess ? LVSA_OK : LVSA_ERR_CUDA;
 }
 
 template <typename T>
 int launch_prologue(const LvsaQkPrologue* a, cudaStream_t s) {
-  const int64_t rows = static_cast<int64_t>(a->batch) * a->seq;
-  const int nv = a->heads * (a->head_dim / 8);
-  const dim3 grid(static_cast<unsigned>((rows + kWarpsPerBlock - 1) / kWarpsPerBlock)), block(32 * kWarpsPerBlock);
-  if (nv <= 32) qk_prologue_kernel<T, 1, true><<<grid, block, 0, s>>>(*a, rows);
-  else if (nv <= 64) qk_prologue_kernel<T, 2, true><<<grid, block, 0, s>>>(*a, rows);
-  else if (nv <= 128) qk_prologue_kernel<T, 4, true><<<grid, block, 0, s>>>(*a, rows);
-  else if (nv <= 256) qk_prologue_kernel<T, 8, true><<<grid, block, 0, s>>>(*a, rows);
-  else if (nv <= 512) qk_prologue_kernel<T, 16, true><<<grid, block, 0, s>>>(*a, rows);
-  else qk_prologue_kernel<T, 32, false><<<grid, block, 0, s>>>(*a, rows);
-  return cudaGetLastError() == cudaSuccess ? LVSA_OK : LVSA_ERR_CUDA;
+  if (a->weight_dtype == LVSA_DTYPE_F32 || a->weight == nullptr) return launch_prologue_t<T, float>(a, s);
+  if (a->weight_dtype == LVSA_DTYPE_BF16) return launch_prologue_t<T, __nv_bfloat16>(a, s);
+  return launch_prologue_t<T, __half>(a, s);
 }
 
 }  // namespace
