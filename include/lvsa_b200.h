@@ -118,6 +118,13 @@ typedef struct LvsaAttnArgs {
   const int32_t* tile_indices;
   const uint8_t* tile_flags;
   int32_t* error_word; /* optional device int: LVSA_ERR_DEVICE_TIMEOUT on a stalled wait */
+  /* Sequence shards (context parallelism, ABI 101): the video segment holds
+   * global tokens [token_offset, token_offset + n_video) of the T x P grid;
+   * frames of query and key tokens are counted from there.  A whole
+   * sequence is token_offset 0 and n_video = T x P. */
+  int32_t token_offset;
+  /* First tile-CSR row to compute (rows [first_q_tile, n_q_tiles)); 0: all. */
+  int32_t first_q_tile;
 } LvsaAttnArgs;
 
 /* Block-sparse attention forward on tcgen05/TMEM, K/V read in place.

@@ -69,7 +69,7 @@ class LvsaAttnArgs(ctypes.Structure):
                 ("block_q", _i32), ("block_k", _i32), ("n_q_video_tiles", _i32),
                 ("n_q_tiles", _i32), ("n_k_video_tiles", _i32),
                 ("frame_bits", _vp), ("tile_indptr", _vp), ("tile_indices", _vp),
-                ("tile_flags", _vp), ("error_word", _vp)]
+                ("tile_flags", _vp), ("error_word", _vp), ("token_offset", _i32), ("first_q_tile", _i32)]
 
 
 class LvsaQkPrologue(ctypes.Structure):

@@ -278,7 +278,8 @@ def block_sparse_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, ma
         mask.total_frames, mask.num_patches, mask.frame_words, mask.block_q, mask.block_k,
         mask.n_q_video_tiles, mask.n_q_tiles, mask.n_k_video_tiles,
         mask.frame_bits.data_ptr(), mask.tile_indptr.data_ptr(), mask.tile_indices.data_ptr(),
-        mask.tile_flags.data_ptr(), error_word(q.device).data_ptr())
+        mask.tile_flags.data_ptr(), error_word(q.device).data_ptr(),
+        getattr(mask, "token_offset", 0), getattr(mask, "first_q_tile", 0))
     with torch.cuda.device(q.device):
         if fp8:
             st = N.load().lvsa_attn_fwd_fp8(ctypes.byref(args), ctypes.byref(sc_c), _stream_ptr(q.device))

@@ -86,6 +86,8 @@ struct AttnParams {
   const float* tvs;
   const float* vref;
   int nqt_all, nkt;  // query / key tiles of the text segment
+  int tok_off;       // global token of the video segment's first token (sequence shards)
+  int row0;          // first tile-CSR row of this launch
 };
 
 
@@ -135,10 +137,11 @@ __device__ __forceinline__ void tile_mask(uint32_t (&am)[4], const AttnParams& p
   } else if (text_row) {
     set_cols(am, 0, min(kBN, prm.n_video - kt * kBN));
   } else {
+    // Key tokens are numbered from the shard start; frames from the grid start.
     const int ks = kt * kBN, kend = min(ks + kBN, prm.n_video);
-    int f = ks / prm.P, c0 = 0;
+    int f = (prm.tok_off + ks) / prm.P, c0 = 0;
     while (ks + c0 < kend) {
-      const int ce = min((f + 1) * prm.P, kend) - ks;
+      const int ce = min((f + 1) * prm.P - prm.tok_off, kend) - ks;
       if ((fbits[f >> 5] >> (f & 31)) & 1u) set_cols(am, c0, ce);
       c0 = ce;
       ++f;
@@ -284,7 +287,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* never = reinterpret_cast<volatile int*>(smem + L::kMisc + 8);  // stays 0: drain waits
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int row = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int row = blockIdx.x + prm.row0, h = blockIdx.y, b = blockIdx.z;
   const int beg = prm.indptr[row];
   const int n = prm.indptr[row + 1] - beg;
   const bool text_row = row >= prm.nqv;
@@ -424,7 +427,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int seg_len = text_row ? prm.n_text : prm.n_video;
     const int tok = tok0 + r;
     const bool valid = tok < seg_len;
-    const int fq = text_row ? 0 : min(tok / prm.P, prm.T - 1);
+    const int fq = text_row ? 0 : min((prm.tok_off + tok) / prm.P, prm.T - 1);
     const uint32_t* fbits = prm.frame_bits + static_cast<size_t>(fq) * prm.words;
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const uint32_t tSc = tS + cls * 128 + lane_base;  // my S / P buffer
@@ -681,7 +684,10 @@ int launch(const LvsaAttnArgs* a, cudaStream_t stream, const LvsaFp8Scales* sc =
   auto kern = lvsa_attn_kernel<D, STAGES, kBf16_, kFp8>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes) != cudaSuccess)
     return LVSA_ERR_CUDA;
-  const int rows = text_rows ? a->n_q_tiles : a->n_q_video_tiles;
+  p.tok_off = a->token_offset;
+  p.row0 = a->first_q_tile;
+  const int rows = (text_rows ? a->n_q_tiles : a->n_q_video_tiles) - a->first_q_tile;
+  if (rows <= 0) return LVSA_OK;
   dim3 grid(rows, a->heads, a->batch);
   kern<<<grid, kThreads, L::kBytes, stream>>>(mq, mk, mv, mtq, mtk, mtv, p);
   return cudaGetLastError() == cudaSuccess ? LVSA_OK : LVSA_ERR_CUDA;
@@ -700,9 +706,13 @@ int validate(const LvsaAttnArgs* a) {
       a->heads % a->kv_heads)
     return LVSA_ERR_INVALID_ARG;
   if (a->block_q != kBlockQ || a->block_k != kBN) return LVSA_ERR_UNSUPPORTED;
-  if (a->total_frames < 1 || a->num_patches < 1 ||
-      static_cast<long long>(a->total_frames) * a->num_patches != a->n_video)
+  // The video segment is the T x P grid or, for a sequence shard, the token
+  // range [token_offset, token_offset + n_video) inside it.
+  const long long grid_tokens = static_cast<long long>(a->total_frames) * a->num_patches;
+  if (a->total_frames < 1 || a->num_patches < 1 || a->token_offset < 0 ||
+      a->token_offset + static_cast<long long>(a->n_video) > grid_tokens)
     return LVSA_ERR_GEOMETRY;
+  if (a->first_q_tile < 0 || a->first_q_tile > a->n_q_tiles) return LVSA_ERR_INVALID_ARG;
   if (a->n_q_video_tiles != (a->n_video + kBlockQ - 1) / kBlockQ || a->n_k_video_tiles != (a->n_video + kBN - 1) / kBN ||
       a->frame_words != (a->total_frames + 31) / 32)
     return LVSA_ERR_GEOMETRY;
@@ -753,4 +763,4 @@ extern "C" const char* lvsa_status_str(int status) {
   }
 }
 
-extern "C" int lvsa_abi_version(void) { return 100; }
+extern "C" int lvsa_abi_version(void) { return 101; }

@@ -411,3 +411,51 @@ def norm_rope(x, norm, weight=None, bias=None, eps=1e-6, cos=None, sin=None, rop
         out[..., 1::2] = x0 * s + x1 * c
         f = out
     return f
+
+
+# ---------------------------------------------------------------------------
+# Reference context parallelism (world > 1): one rank's output.
+def attention_cp(q, k, v, k_full, v_full, T, P, W, n_first, kfi, offset, rank, world, expand=True,
+                 text_q=None, text_k=None, text_v=None, scale=None):
+    """The reference's sequence-sharded LVSA on rank ``rank`` of ``world``.
+
+    q/k/v [B, S_r, H(kv), D] are this rank's tokens; k_full/v_full [B, T*P,
+    Hkv, D] the whole sequence, from which the global frames are taken (what
+    ``_build_global_kv``'s all_reduce assembles, lvsa/lvsa_processor.py:
+    643-706).  Globals = user keyframes + boundary guards
+    (lvsa/lvsa_processor.py:131-137, lvsa/sparse_attention.py:107-129).
+    Video rows of local frame f attend [global frames; text] + the parts of
+    f's window frames (globals excluded) that are on this rank
+    (lvsa/sparse_attention.py:389-402, 643-706, processor :545-549); text rows
+    attend [this rank's video keys; text] (processor :586-591).
+    Returns (out [B, S_r, H, D], text_out or None), float32."""
+    B, S_r, H, D = q.shape
+    Hkv = k.shape[2]
+    rep = H // Hkv
+    sc = scale if scale is not None else 1.0 / np.sqrt(D)
+    guards = compute_boundary_guard_frames(T, T * P // world, P, world, W)
+    fp = frame_pattern(T, P, W, n_first, kfi, offset, expand, rank, world, boundary_guards=guards)
+    g = [int(x) for x in np.nonzero(fp["global_frame_mask"])[0]]
+    gidx = np.concatenate([np.arange(f * P, (f + 1) * P) for f in g]) if g else np.zeros(0, dtype=np.int64)
+    out = np.zeros((B, S_r, H, D), dtype=np.float32)
+    for b in range(B):
+        kg, vg = k_full[b][gidx], v_full[b][gidx]
+        if text_k is not None:
+            kg, vg = np.concatenate([kg, text_k[b]]), np.concatenate([vg, text_v[b]])
+        for f, s, e in fp["local_frames"]:
+            parts = fp["window_ctx"][f]
+            kc = np.concatenate([kg] + [k[b][ps:pe] for ps, pe in parts])
+            vc = np.concatenate([vg] + [v[b][ps:pe] for ps, pe in parts])
+            for h in range(H):
+                out[b, s:e, h] = _softmax_av(q[b, s:e, h].astype(np.float32), kc[:, h // rep].astype(np.float32),
+                                             vc[:, h // rep].astype(np.float32), sc)
+    tout = None
+    if text_q is not None:
+        nt = text_q.shape[1]
+        tout = np.zeros((B, nt, H, D), dtype=np.float32)
+        for b in range(B):
+            kc, vc = np.concatenate([k[b], text_k[b]]), np.concatenate([v[b], text_v[b]])
+            for h in range(H):
+                tout[b, :, h] = _softmax_av(text_q[b, :, h].astype(np.float32), kc[:, h // rep].astype(np.float32),
+                                            vc[:, h // rep].astype(np.float32), sc)
+    return out, tout

@@ -9,7 +9,8 @@ It writes ``patterns.npz`` (frame-level ``LVSAMetadata.build`` outputs),
 ``lvsa_sdpa`` output and dense text-query rows) and ``rope.npz`` (the
 reference's ``apply_rotary_emb`` / ``slice_rotary_emb`` on seeded inputs)
 and ``adapters.npz`` (the reference HunyuanVideo / CogVideoX adapters on
-seeded mock modules); ``--only rope|adapters`` writes just one of them.  The fixtures are committed;
+seeded mock modules) and ``cp.npz`` (the reference's world > 1 path, per
+rank); ``--only rope|adapters|cp`` writes just one of them.  The fixtures are committed;
 the tests never need the reference at run time.
 """
 
@@ -151,6 +152,59 @@ def rope_golden(ref_root: str) -> None:
     print("wrote rope")
 
 
+CP_CASES = [  # name, T, P, H, Hkv, D, W, n_first, kfi, offset, n_text, world, seed
+    ("cp_w2", 9, 40, 2, 2, 64, 1, 1, 4, 1, 17, 2, 71),
+    ("cp_w3_mid", 9, 50, 2, 1, 64, 2, 1, 3, 2, 0, 3, 72),   # rank splits inside frames, GQA
+    ("cp_w4_d128", 12, 30, 2, 2, 128, 1, 1, 5, 0, 9, 4, 73),
+]
+
+
+def cp_golden(ref_root: str) -> None:
+    """The reference's world > 1 path on each rank: LVSAMetadata.build with the
+    processor's boundary guards, the global K/V _build_global_kv assembles
+    (all global frames, text appended), lvsa_sdpa; text queries attend the
+    rank's video keys + text (lvsa/lvsa_processor.py:586-591)."""
+    sys.path.insert(0, ref_root)
+    from lvsa.sparse_attention import LVSAMetadata, compute_boundary_guard_frames, lvsa_sdpa
+    from lvsa.lvsa_processor import DistributedLVSAProcessor
+    arrays = {}
+    for name, T, P, H, Hkv, D, W, nf, kfi, off, nt, world, seed in CP_CASES:
+        g = torch.Generator().manual_seed(seed)
+        N = T * P
+        q = bf16_round(torch.randn(1, N, H, D, generator=g))
+        k = bf16_round(torch.randn(1, N, Hkv, D, generator=g))
+        v = bf16_round(torch.randn(1, N, Hkv, D, generator=g))
+        tq = bf16_round(torch.randn(1, nt, H, D, generator=g))
+        tk = bf16_round(torch.randn(1, nt, Hkv, D, generator=g))
+        tv = bf16_round(torch.randn(1, nt, Hkv, D, generator=g))
+        arrays.update({f"{name}.q": q.numpy(), f"{name}.k": k.numpy(), f"{name}.v": v.numpy(),
+                       f"{name}.text_q": tq.numpy(), f"{name}.text_k": tk.numpy(), f"{name}.text_v": tv.numpy(),
+                       f"{name}.params": np.asarray([T, P, H, Hkv, D, W, nf, kfi, off, nt, world, seed])})
+        S_r = N // world
+        guards = compute_boundary_guard_frames(T, S_r, P, world, W)
+        for r in range(world):
+            m = LVSAMetadata.build(total_latent_frames=T, num_patches=P, window_size=W, n_first_frames=nf,
+                                   key_frame_interval=kfi, rank=r, world=world, expand_window=True,
+                                   keyframe_offset=off, boundary_guards=guards)
+            gi = torch.tensor(m.global_indices, dtype=torch.long)
+            idx = (gi[:, None] * P + torch.arange(P)[None, :]).flatten()
+            kg, vg = k[:, idx], v[:, idx]
+            if nt:
+                kg, vg = torch.cat([kg, tk], 1), torch.cat([vg, tv], 1)
+            sl = slice(r * S_r, (r + 1) * S_r)
+            out = lvsa_sdpa(q[:, sl], k[:, sl], v[:, sl], kg, vg, m)
+            arrays[f"{name}.out{r}"] = out.numpy()
+            arrays[f"{name}.globals{r}"] = np.asarray(m.global_indices)
+            if nt:
+                fk, fv = torch.cat([k[:, sl], tk], 1), torch.cat([v[:, sl], tv], 1)
+                if Hkv != H:
+                    fk, fv = fk.repeat_interleave(H // Hkv, 2), fv.repeat_interleave(H // Hkv, 2)
+                arrays[f"{name}.text_out{r}"] = DistributedLVSAProcessor._compute_full_attention(
+                    None, tq, fk, fv).numpy()
+    np.savez_compressed(os.path.join(HERE, "cp.npz"), **arrays)
+    print("wrote cp")
+
+
 def adapters_golden(ref_root: str) -> None:
     """The reference HunyuanVideo / CogVideoX adapters (lvsa/adapters/
     hunyuan_video.py, cogvideox.py) on seeded mock modules: extract_qkv,
@@ -211,8 +265,9 @@ if __name__ == "__main__":
     root = args[0] if args else os.environ.get("LVSA_REFERENCE_ROOT", ".")
     if "--only" in sys.argv:
         which = sys.argv[sys.argv.index("--only") + 1]
-        {"rope": rope_golden, "adapters": adapters_golden}[which](root)
+        {"rope": rope_golden, "adapters": adapters_golden, "cp": cp_golden}[which](root)
     else:
         main(root)
         rope_golden(root)
         adapters_golden(root)
+        cp_golden(root)

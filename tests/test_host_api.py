@@ -122,7 +122,7 @@ def test_library_exports_every_header_symbol():
     nm = subprocess.run(["nm", "-D", "--defined-only", _native.LIB_PATH], capture_output=True, text=True)
     exported = set(re.findall(r" T (lvsa_\w+)", nm.stdout))
     assert declared <= exported
-    assert lib.lvsa_abi_version() == 100
+    assert lib.lvsa_abi_version() == 101
     assert lib.lvsa_status_str(0) == b"ok"
 
 
