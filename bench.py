@@ -181,7 +181,39 @@ def run_b200(args, cfg):
     T, P, H, D, nt = cfg["T"], cfg["P"], cfg["H"], cfg["D"], cfg["n_text"]
     flop_tiles, flop_exact = flops_for(cfg)
     ulysses = args.parallel == "ulysses" and world > 1
-    if ulysses:
+    refcp = args.parallel == "cp" and world > 1
+    if refcp:
+        # Strong scaling with the reference's own world > 1 pattern: each rank
+        # holds its token shard; global frames (keyframes + boundary guards)
+        # are gathered by one NCCL all-reduce per layer, windows stay local.
+        from longvideosparseattention_b200.cp_mode import GlobalKV, build_shard_pattern, cp_attention
+        if (T * P) % world:
+            raise SystemExit(f"reference CP needs T*P ({T * P}) divisible by the GPU count ({world})")
+        S_r = T * P // world
+        shard = build_shard_pattern(T, P, cfg["W"], cfg["n_first"], cfg["kfi"], cfg["step"] % cfg["kfi"],
+                                    rank, world, nt, device=dev)
+        gkv = GlobalKV()
+        layers = []
+        for i in range(L):
+            lay = seeded_layer(cfg, i, dev)
+            lay[:3] = [x[:, rank * S_r:(rank + 1) * S_r].contiguous() for x in lay[:3]]
+            layers.append(lay)
+            del lay
+        torch.cuda.empty_cache()
+        # Useful FLOPs of this rank's pattern (clipped tile areas, dense terms exact), summed over ranks.
+        ip, ix = shard.video.tile_indptr.cpu().numpy(), shard.video.tile_indices.cpu().numpy()
+        area = 0
+        for qt in range(shard.video.n_q_video_tiles):
+            rows_q = min(S_r, (qt + 1) * 128) - qt * 128
+            for kt in ix[ip[qt]:ip[qt + 1]]:
+                if kt < shard.video.n_k_video_tiles:
+                    area += rows_q * (min(S_r, (int(kt) + 1) * 128) - int(kt) * 128)
+        n_dense = len(shard.global_indices) * P + nt
+        cp_flop = 4 * D * H * (area + S_r * n_dense + nt * (S_r + nt))
+        tt = torch.tensor([cp_flop], dtype=torch.float64, device=dev)
+        dist.all_reduce(tt)
+        flop_tiles = float(tt.item())
+    elif ulysses:
         # Strong scaling: the same 30 layers on every N; each rank holds its
         # contiguous token shard of q/k/v (heads are scattered by all-to-all).
         from longvideosparseattention_b200.ulysses import shard_sizes, ulysses_attention
@@ -212,7 +244,9 @@ def run_b200(args, cfg):
             if ev is not None:
                 ev[i][0].record(stream)
             tx = (lay[3], lay[4], lay[5]) if nt else (None, None, None)
-            if ulysses:
+            if refcp:
+                cp_attention(lay[0], lay[1], lay[2], shard, gkv, *tx)
+            elif ulysses:
                 ulysses_attention(lay[0], lay[1], lay[2], sizes,
                                   lambda q, k, v, a, b_, c: block_sparse_attention(q, k, v, mask, a, b_, c), *tx)
             else:
@@ -248,25 +282,25 @@ def run_b200(args, cfg):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_max = float(t.item())
     ms_step = ms_max / args.steps
-    total_flop = flop_tiles * L * args.steps * (1 if ulysses else world)
+    total_flop = flop_tiles * L * args.steps * (1 if (ulysses or refcp) else world)
     value = total_flop / (ms_max * 1e-3) / 1e12
 
     # ---- e2e through the public API with pinned host buffers (copies inside the timed region)
     e2e = None
-    if not args.no_e2e and not ulysses:
+    if not args.no_e2e and not (ulysses or refcp):
         e2e = run_e2e(args, cfg, dev, world, flop_tiles)
 
     if rank == 0:
         pk, pk_kind = peaks()
         mean_launch = statistics.mean(kern_ms)
         # per timed layer call: H/world heads under Ulysses (all-to-all included)
-        achieved = flop_tiles / (world if ulysses else 1) / (mean_launch * 1e-3) / 1e12
+        achieved = flop_tiles / (world if (ulysses or refcp) else 1) / (mean_launch * 1e-3) / 1e12
         peak = pk.get("bf16_tflops_sustained", pk.get("bf16_tflops"))
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 3),
             "ms_per_layer": round(ms_step / L, 4), "higher_is_better": True,
-            "scaling": "strong" if ulysses else "weak",
+            "scaling": "strong" if (ulysses or refcp) else "weak",
             "vs_baseline": None, "dtype": "e4m3 (QK, PV; fp32 accumulate)" if args.fp8 else "bf16",
             "data": "synthetic (seeded N(0,1)/sqrt(D), RoPE-3D)",
             "config": {"workload": args.config, "desc": cfg["desc"], "layers_per_step": L,
@@ -274,6 +308,8 @@ def run_b200(args, cfg):
                        "flop_tiles_per_layer": flop_tiles, "flop_exact_per_layer": flop_exact,
                        "l2": "30 distinct layer inputs (35 GB) cycled: inputs exceed L2, no flush",
                        "parallelism": (f"ulysses x{world} (heads scattered by NCCL all-to-all)" if ulysses
+                                       else (f"reference CP x{world} (token shards, global frames by NCCL "
+                                             "all-reduce, rank-local windows; FLOPs of that pattern)") if refcp
                                        else f"replicas x{world} (independent layers per rank)")},
             "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak,
                          "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
@@ -282,7 +318,7 @@ def run_b200(args, cfg):
                          "peak_source": f"{pk_kind} bf16_tflops_sustained (kernel runs back-to-back in a long step)",
                          "mean_launch_ms": round(mean_launch, 4)},
             "clocks": clk.summary(),
-            "gpu_launches": (4 + L * (7 if args.fp8 else 1)) * args.steps,
+            "gpu_launches": (4 + L * (7 if args.fp8 else (2 if refcp and nt else 1))) * args.steps,
             "e2e": e2e,
         }
         if args.cpu_baseline:
@@ -493,9 +529,10 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--fp8", action="store_true",
                     help="E4M3 QK/PV with per-tile scales (quantisation inside the timed step)")
-    ap.add_argument("--parallel", default="replicas", choices=["replicas", "ulysses"],
-                    help="N>1: independent layers per rank (weak scaling) or Ulysses head "
-                         "parallelism over one set of layers (strong scaling)")
+    ap.add_argument("--parallel", default="replicas", choices=["replicas", "ulysses", "cp"],
+                    help="N>1: independent layers per rank (weak scaling), Ulysses head "
+                         "parallelism over one set of layers (strong scaling), or the reference's "
+                         "own sequence-shard pattern (cp, strong scaling)")
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--prologue", action="store_true",

@@ -9,10 +9,11 @@ gather, K/V concatenation, FlashInfer plan / compact copy / LSE merge and the
 separate dense encoder SDPA all disappear.
 
 Multi-GPU: with ``world > 1`` the processor expects sequence-sharded hidden
-states (as the reference) and runs Ulysses head parallelism
-(``ulysses.ulysses_attention``) with the world = 1 pattern on every rank.  The
-reference's own world > 1 pattern (boundary-guard anchors, rank-local windows)
-is not reproduced.
+states (as the reference).  ``cp_mode="ulysses"`` (default) runs Ulysses head
+parallelism (``ulysses.ulysses_attention``) with the world = 1 pattern on
+every rank; ``cp_mode="reference"`` reproduces the reference's own world > 1
+pattern (boundary-guard anchors gathered by one all-reduce, rank-local
+windows, ``cp_mode.cp_attention``).
 """
 
 from __future__ import annotations
@@ -37,7 +38,12 @@ class DistributedLVSAProcessor:
     def __init__(self, total_num_latent_frames: int, num_patches: int, window_size: int,
                  n_first_frames: int, key_frame_interval: Optional[int], rank: int, world: int,
                  expand_window: bool = True, adapter: Optional[ModelAdapter] = None,
-                 sparsity_scale: float = 1.0, reference_frames: int = 21) -> None:
+                 sparsity_scale: float = 1.0, reference_frames: int = 21, cp_mode: str = "ulysses") -> None:
+        if cp_mode not in ("ulysses", "reference"):
+            raise ValueError(f"cp_mode must be 'ulysses' or 'reference', got {cp_mode!r}")
+        self.cp_mode = cp_mode
+        self._shard = None  # reference-mode shard pattern (per step, built lazily on the device)
+        self._global_kv = None
         self.total_num_frames = total_num_latent_frames
         self.num_patches = num_patches
         self.window_size = window_size
@@ -51,8 +57,9 @@ class DistributedLVSAProcessor:
             from .adapters.wan import WanAdapter
             adapter = WanAdapter()
         self.adapter = adapter
-        # Kept for API parity (lvsa/lvsa_processor.py:133-137); the Ulysses
-        # path uses the world = 1 pattern, so these are not made anchors.
+        # lvsa/lvsa_processor.py:131-137.  cp_mode="reference" makes them
+        # anchors (build_shard_pattern derives the same list); the Ulysses
+        # path uses the world = 1 pattern, where they are not anchors.
         self._boundary_guards: List[int] = compute_boundary_guard_frames(
             total_num_latent_frames, total_num_latent_frames * num_patches // world,
             num_patches, world, window_size)
@@ -85,6 +92,7 @@ class DistributedLVSAProcessor:
         self._fi_MB = m.fi_MB
         self._fi_compact_n = m.fi_compact_n
         self._block_mask = None  # GPU tile CSR, rebuilt lazily (reusing its buffers)
+        self._shard = None
 
     def _rebuild_for_current_params(self, offset: int) -> None:
         """Recompute the pattern for the current window / kfi / offset
@@ -148,6 +156,17 @@ class DistributedLVSAProcessor:
 
     # --------------------------------------------------------------- forward
     def _attend(self, query, key, value, enc_q, enc_k, enc_v):
+        if self.world > 1 and self.cp_mode == "reference":
+            from .cp_mode import GlobalKV, build_shard_pattern, cp_attention
+            nt = 0 if enc_k is None else int(enc_k.shape[1])
+            m = self._metadata
+            if self._shard is None or self._shard.n_text != nt or self._shard.video.tile_indptr.device != query.device:
+                self._shard = build_shard_pattern(m.total_latent_frames, m.num_patches, m.window_size,
+                                                  m.n_first_frames, m.key_frame_interval, m.keyframe_offset,
+                                                  self.rank, self.world, nt, m.expand_window, device=query.device)
+            if self._global_kv is None:
+                self._global_kv = GlobalKV()
+            return cp_attention(query, key, value, self._shard, self._global_kv, enc_q, enc_k, enc_v)
         if self.world == 1:
             nt = 0 if enc_k is None else int(enc_k.shape[1])
             return block_sparse_attention(query, key, value, self.block_mask(query.device, nt),

@@ -115,3 +115,14 @@ def test_processor_dense_fallback_on_geometry_mismatch(capsys):
         out = proc(attn, x)
     assert out.shape == x.shape and torch.isfinite(out.float()).all()
     assert "geometry mismatch" in capsys.readouterr().out
+
+
+def test_cp_mode_option_and_shard_invalidation():
+    from longvideosparseattention_b200.lvsa_processor import DistributedLVSAProcessor
+    with pytest.raises(ValueError):
+        DistributedLVSAProcessor(9, 40, 1, 1, 4, 0, 2, cp_mode="ring")
+    p = DistributedLVSAProcessor(9, 40, 1, 1, 4, 0, 2, cp_mode="reference")
+    assert p.cp_mode == "reference" and p._shard is None
+    p._shard = object()
+    p.set_step(1)  # rotation: the shard pattern is rebuilt lazily
+    assert p._shard is None
