@@ -329,10 +329,13 @@ def run_b200(args, cfg):
 
 
 def run_e2e(args, cfg, dev, world, flop_tiles):
-    """Public-API path with host tensors: per layer, H2D of q/k/v(+text) from
-    pinned memory, the attention call, D2H of the output, all in the timed region."""
+    """Public-API path with host tensors (``pipeline.attention_from_host``):
+    per layer, H2D of q/k/v(+text) from pinned memory, the attention call, D2H
+    of the output, all in the timed region; the copies of neighbouring layers
+    overlap the kernel on separate streams."""
     import torch
-    from longvideosparseattention_b200 import block_sparse_attention, build_block_mask
+    from longvideosparseattention_b200 import build_block_mask
+    from longvideosparseattention_b200.pipeline import attention_from_host
     L, nt = cfg["layers"], cfg["n_text"]
     host = []
     for i in range(2):  # two distinct pinned layer inputs, cycled
@@ -348,13 +351,8 @@ def run_e2e(args, cfg, dev, world, flop_tiles):
     def step():
         mask = build_block_mask(cfg["T"], cfg["P"], cfg["W"], cfg["n_first"], cfg["kfi"],
                                 cfg["step"] % cfg["kfi"], True, nt, device=dev)
-        for i in range(L):
-            d = [x.to(dev, non_blocking=True) for x in host[i & 1]]
-            tx = (d[3], d[4], d[5]) if nt else (None, None, None)
-            o, to = block_sparse_attention(d[0], d[1], d[2], mask, *tx)
-            out_h.copy_(o, non_blocking=True)
-            if nt:
-                tout_h.copy_(to, non_blocking=True)
+        ins = [tuple(host[i & 1]) if nt else tuple(host[i & 1][:3]) + (None, None, None) for i in range(L)]
+        attention_from_host(ins, mask, [(out_h, tout_h)] * L, dev)
         return mask
 
     steps = max(1, min(args.steps, 3))
