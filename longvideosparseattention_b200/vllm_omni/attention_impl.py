@@ -16,11 +16,21 @@ import torch.nn.functional as F
 from ..block_sparse import block_sparse_attention
 from ..sparse_attention import LVSAMetadata, compute_auto_kfi
 from . import step_tracker
+from ._fallback import warn_fallback
 from .config import LVSAConfig, candidate_patches_per_frame
+
+
+def _reset_step_counter() -> None:
+    """Called by ``step_tracker.reset()``: drop the shared call counter so a
+    calibration does not carry over between generations."""
+    step_tracker._global_tracker = None
 
 
 class LVSAAttentionImpl:
     _total_instances = 0
+    # Set by the block-level hooks: they run the sparse path themselves, so
+    # the backend's own forward keeps to dense attention.
+    _hook_active = False
 
     def __init__(self, num_heads: int, head_size: int, softmax_scale: float, causal: bool = False,
                  num_kv_heads: Optional[int] = None, prefix: str = "", qkv_layout: Optional[str] = None,
@@ -77,13 +87,17 @@ class LVSAAttentionImpl:
     @torch.compiler.disable
     def forward_cuda(self, query: torch.Tensor, key: torch.Tensor, value: torch.Tensor,
                      attn_metadata: Any = None) -> torch.Tensor:
+        if LVSAAttentionImpl._hook_active:
+            return self._dense_attention(query, key, value)
         if query.shape[1] != key.shape[1]:
             return self._dense_attention(query, key, value)  # cross-attention
         T = self._total_frames()
         if T is None:
+            warn_fallback("forward_cuda", "no_t_lat", query.shape[1])
             return self._dense_attention(query, key, value)
         P, text = self.detect_geometry(query.shape[1], T)
         if P is None:
+            warn_fallback("forward_cuda", "geometry_detect", query.shape[1], {"T_lat": T})
             return self._dense_attention(query, key, value)
         meta = self._metadata(T, P)
         nv = T * P
