@@ -248,7 +248,8 @@ def run_b200(args, cfg):
                 cp_attention(lay[0], lay[1], lay[2], shard, gkv, *tx)
             elif ulysses:
                 ulysses_attention(lay[0], lay[1], lay[2], sizes,
-                                  lambda q, k, v, a, b_, c: block_sparse_attention(q, k, v, mask, a, b_, c), *tx)
+                                  lambda q, k, v, a, b_, c: block_sparse_attention(q, k, v, mask, a, b_, c), *tx,
+                                  chunks=args.chunks)
             else:
                 block_sparse_attention(lay[0], lay[1], lay[2], mask, *tx, out=outs[i & 1], text_out=touts[i & 1],
                                        fp8=args.fp8)
@@ -307,7 +308,8 @@ def run_b200(args, cfg):
                        "tokens": T * P + nt, "heads": H, "head_dim": D, "tile": "128x128",
                        "flop_tiles_per_layer": flop_tiles, "flop_exact_per_layer": flop_exact,
                        "l2": "30 distinct layer inputs (35 GB) cycled: inputs exceed L2, no flush",
-                       "parallelism": (f"ulysses x{world} (heads scattered by NCCL all-to-all)" if ulysses
+                       "parallelism": (f"ulysses x{world} (heads scattered by NCCL all-to-all, "
+                                        f"chunks={args.chunks or 'auto'})" if ulysses
                                        else (f"reference CP x{world} (token shards, global frames by NCCL "
                                              "all-reduce, rank-local windows; FLOPs of that pattern)") if refcp
                                        else f"replicas x{world} (independent layers per rank)")},
@@ -533,6 +535,8 @@ def main():
                          "own sequence-shard pattern (cp, strong scaling)")
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--chunks", type=int, default=None,
+                    help="Ulysses: head groups exchanged while the previous group computes (default: auto)")
     ap.add_argument("--prologue", action="store_true",
                     help="time the fused QK prologue (norm + RoPE) instead of the attention step")
     args = ap.parse_args()

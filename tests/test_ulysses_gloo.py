@@ -30,7 +30,7 @@ def _case(B, T, P, H, D, nt, seed=0):
             mk(B, nt, H, D), mk(B, nt, H, D), mk(B, nt, H, D))
 
 
-def _worker(rank, world, port, B, T, P, H, D, nt, W, kfi, off, q_ret):
+def _worker(rank, world, port, B, T, P, H, D, nt, W, kfi, off, q_ret, chunks=None):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
@@ -49,19 +49,24 @@ def _worker(rank, world, port, B, T, P, H, D, nt, W, kfi, off, q_ret):
             return torch.from_numpy(o), (None if to is None else torch.from_numpy(to))
 
         out, tout = ulysses_attention(q[:, sl], k[:, sl], v[:, sl], sizes, local,
-                                      tq if nt else None, tk if nt else None, tv if nt else None)
+                                      tq if nt else None, tk if nt else None, tv if nt else None,
+                                      chunks=chunks)
         q_ret.put((rank, out.numpy(), None if tout is None else tout.numpy()))
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,B,T,P,H,nt", [(2, 1, 7, 10, 4, 6), (3, 1, 5, 11, 6, 0), (2, 2, 6, 9, 2, 5)])
-def test_ulysses_matches_world1(world, B, T, P, H, nt):
+@pytest.mark.parametrize("world,B,T,P,H,nt,chunks", [(2, 1, 7, 10, 4, 6, None), (3, 1, 5, 11, 6, 0, None),
+                                                     (2, 2, 6, 9, 2, 5, None), (2, 1, 5, 12, 12, 7, 3),
+                                                     (3, 2, 4, 9, 6, 4, 1)])
+def test_ulysses_matches_world1(world, B, T, P, H, nt, chunks):
+    """Head groups exchanged and computed one after another (chunks) give the
+    same rows as one exchange."""
     D, W, kfi, off = 16, 1, 3, 1
     ctx = mp.get_context("spawn")
     qret = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, B, T, P, H, D, nt, W, kfi, off, qret))
+    procs = [ctx.Process(target=_worker, args=(r, world, port, B, T, P, H, D, nt, W, kfi, off, qret, chunks))
              for r in range(world)]
     for p in procs:
         p.start()
