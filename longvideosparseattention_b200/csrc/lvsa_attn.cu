@@ -91,16 +91,16 @@ struct AttnParams {
 };
 
 
-template <int D, int STAGES, bool kFp8 = false>
+template <int D, int SK, int SV, bool kFp8 = false>
 struct Smem {
   static constexpr int kElem = kFp8 ? 1 : 2;       // bytes per element
   static constexpr int kCh = D * kElem / 128;      // 128-byte column slabs per row
   static constexpr int kTile = kCh * kChunk;       // bytes of one 128 x D tile
   static constexpr int kQ = 0;                     // query tile; the epilogue's merge buffer afterwards
   static constexpr int kK = kQ + kTile;
-  static constexpr int kV = kK + STAGES * kTile;
-  static constexpr int kBar = kV + STAGES * kTile;
-  static constexpr int kNumBars = 4 * STAGES + 8;
+  static constexpr int kV = kK + SK * kTile;
+  static constexpr int kBar = kV + SV * kTile;
+  static constexpr int kNumBars = 2 * SK + 2 * SV + 8;
   static constexpr int kMisc = kBar + kNumBars * 8;
   static constexpr int kBytes = kMisc + 16 + 1024;  // + alignment slack
   static_assert(kBytes <= 232448, "shared memory");
@@ -260,13 +260,13 @@ __device__ __forceinline__ void store_p(uint32_t taddr, const uint32_t (&pk)[32]
 
 // kBf16: type of O (and of Q/K/V unless kFp8).  kFp8: Q/K/V are E4M3 copies
 // with per-tile scales (QK^T and PV on kind::f8f6f4, P rounded to E4M3).
-template <int D, int STAGES, bool kBf16, bool kFp8 = false>
+template <int D, int SK, int SV, bool kBf16, bool kFp8 = false>
 __global__ void __launch_bounds__(kThreads, 1)
     lvsa_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                      const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_tq,
                      const __grid_constant__ CUtensorMap tm_tk, const __grid_constant__ CUtensorMap tm_tv,
                      const AttnParams prm) {
-  using L = Smem<D, STAGES, kFp8>;
+  using L = Smem<D, SK, SV, kFp8>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem + L::kQ;
@@ -275,10 +275,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBar);
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;
-  uint64_t* v_full = k_full + STAGES;
-  uint64_t* k_empty = v_full + STAGES;   // K stage free: the S of its tile is done
-  uint64_t* v_empty = k_empty + STAGES;  // V stage free: the PV of its tile is done
-  uint64_t* s_full = v_empty + STAGES;   // [2] S buffer c holds S(j), j % 2 == c
+  uint64_t* v_full = k_full + SK;       // [SV]
+  uint64_t* k_empty = v_full + SV;       // [SK] K stage free: the S of its tile is done
+  uint64_t* v_empty = k_empty + SK;      // [SV] V stage free: the PV of its tile is done
+  uint64_t* s_full = v_empty + SV;       // [2] S buffer c holds S(j), j % 2 == c
   uint64_t* p_full = s_full + 2;         // [2] P(j) written into buffer c
   uint64_t* o_done = p_full + 2;         // every MMA of the CTA retired
   uint64_t* drain = o_done + 1;
@@ -296,10 +296,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < SK; ++s) {
       mbar_init(&k_full[s], 1);
-      mbar_init(&v_full[s], 1);
       mbar_init(&k_empty[s], 1);
+    }
+    for (int s = 0; s < SV; ++s) {
+      mbar_init(&v_full[s], 1);
       mbar_init(&v_empty[s], 1);
     }
     for (int i = 0; i < 2; ++i) {
@@ -334,34 +336,34 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int c = 0; c < L::kCh; ++c) tma_load_4d(sQ + c * kChunk, mq, q_full, c * (128 / L::kElem), h, tok0, b);
       int k_issued = 0, v_issued = 0;
       for (int j = 0; j < n; ++j) {
-        const int s = j % STAGES;
+        const int s = j % SK, sv = j % SV;
         const int kt = prm.indices[beg + j];
         const bool tt = kt >= prm.nkv;
         const int ktok = (tt ? kt - prm.nkv : kt) * kBN;
         const CUtensorMap* mk = tt ? &tm_tk : &tm_k;
         const CUtensorMap* mv = tt ? &tm_tv : &tm_v;
-        if (j >= STAGES && !mbar_wait(&k_empty[s], ((j / STAGES) - 1) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT))
+        if (j >= SK && !mbar_wait(&k_empty[s], ((j / SK) - 1) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT))
           break;
         mbar_expect_tx(&k_full[s], L::kTile);
 #pragma unroll
         for (int c = 0; c < L::kCh; ++c)
           tma_load_4d(sK + s * L::kTile + c * kChunk, mk, &k_full[s], c * (128 / L::kElem), hk, ktok, b);
         k_issued = j + 1;
-        if (j >= STAGES && !mbar_wait(&v_empty[s], ((j / STAGES) - 1) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT))
+        if (j >= SV && !mbar_wait(&v_empty[sv], ((j / SV) - 1) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT))
           break;
-        mbar_expect_tx(&v_full[s], L::kTile);
+        mbar_expect_tx(&v_full[sv], L::kTile);
 #pragma unroll
         for (int c = 0; c < L::kCh; ++c)
-          tma_load_4d(sV + s * L::kTile + c * kChunk, mv, &v_full[s], c * (128 / L::kElem), hk, ktok, b);
+          tma_load_4d(sV + sv * L::kTile + c * kChunk, mv, &v_full[sv], c * (128 / L::kElem), hk, ktok, b);
         v_issued = j + 1;
       }
       if (*abort) {
         // Drain our own copies still in flight before the CTA retires.
         mbar_wait(q_full, 0, never, nullptr, 0);
-        for (int j = max(0, k_issued - STAGES); j < k_issued; ++j)
-          mbar_wait(&k_full[j % STAGES], (j / STAGES) & 1, never, nullptr, 0);
-        for (int j = max(0, v_issued - STAGES); j < v_issued; ++j)
-          mbar_wait(&v_full[j % STAGES], (j / STAGES) & 1, never, nullptr, 0);
+        for (int j = max(0, k_issued - SK); j < k_issued; ++j)
+          mbar_wait(&k_full[j % SK], (j / SK) & 1, never, nullptr, 0);
+        for (int j = max(0, v_issued - SV); j < v_issued; ++j)
+          mbar_wait(&v_full[j % SV], (j / SV) & 1, never, nullptr, 0);
       }
     }
   } else if (warp == kMmaWarp) {
@@ -374,14 +376,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t idO = idesc_f16(kBM, D, kFmt1, true);
       const uint32_t q_base = smem_u32(sQ), k_base = smem_u32(sK), v_base = smem_u32(sV);
       auto issue_s = [&](int jj) {
-        const uint32_t kb = k_base + (jj % STAGES) * L::kTile, dS = tS + (jj & 1) * 128;
+        const uint32_t kb = k_base + (jj % SK) * L::kTile, dS = tS + (jj & 1) * 128;
 #pragma unroll
         for (int kk = 0; kk < D * L::kElem / 32; ++kk) {  // 32 bytes of Q and K per instruction
           const uint32_t off = (kk >> 2) * kChunk + (kk & 3) * 32;
           mma_ss_any<kFp8>(dS, sdesc_sw128(q_base + off, 16, 1024), sdesc_sw128(kb + off, 16, 1024), idS, kk > 0);
         }
         mma_commit(&s_full[jj & 1]);
-        mma_commit(&k_empty[jj % STAGES]);
+        mma_commit(&k_empty[jj % SK]);
       };
       bool ok = mbar_wait(q_full, 0, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT) &&
                 mbar_wait(&k_full[0], 0, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT);
@@ -389,7 +391,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         issue_s(0);
       }
-      if (ok && n > 1 && (ok = mbar_wait(&k_full[1 % STAGES], (1 / STAGES) & 1, abort, prm.err,
+      if (ok && n > 1 && (ok = mbar_wait(&k_full[1 % SK], (1 / SK) & 1, abort, prm.err,
                                          LVSA_ERR_DEVICE_TIMEOUT))) {
         tc_fence_after();
         issue_s(1);
@@ -397,17 +399,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int j = 0; ok && j < n; ++j) {
         const int c = j & 1, it = j >> 1;
         if (!(ok = mbar_wait(&p_full[c], it & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT))) break;
-        if (!(ok = mbar_wait(&v_full[j % STAGES], (j / STAGES) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT))) break;
+        if (!(ok = mbar_wait(&v_full[j % SV], (j / SV) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT))) break;
         tc_fence_after();
-        const uint32_t vb = v_base + (j % STAGES) * L::kTile, pa = tS + c * 128, dO = tO + c * 128;
+        const uint32_t vb = v_base + (j % SV) * L::kTile, pa = tS + c * 128, dO = tO + c * 128;
 #pragma unroll
         for (int kk = 0; kk < kBN * L::kElem / 32; ++kk)  // 32 / kElem keys per instruction
           mma_ts_any<kFp8>(dO, pa + kk * 8, sdesc_sw128(vb + kk * (32 / L::kElem) * 128, kChunk, 1024), idO,
                            (it > 0 || kk > 0));
-        mma_commit(&v_empty[j % STAGES]);
+        mma_commit(&v_empty[j % SV]);
         if (j + 2 < n) {
           // S buffer c: P(j) was read by PV(j), issued just before.
-          if (!(ok = mbar_wait(&k_full[(j + 2) % STAGES], ((j + 2) / STAGES) & 1, abort, prm.err,
+          if (!(ok = mbar_wait(&k_full[(j + 2) % SK], ((j + 2) / SK) & 1, abort, prm.err,
                                LVSA_ERR_DEVICE_TIMEOUT)))
             break;
           tc_fence_after();
@@ -631,9 +633,9 @@ int make_map(CUtensorMap* map, const LvsaTensor& t, int B, int N, int Hx, int D,
   return r == CUDA_SUCCESS ? LVSA_OK : LVSA_ERR_ALIGNMENT;
 }
 
-template <int D, int STAGES, bool kBf16_, bool kFp8 = false>
+template <int D, int SK, int SV, bool kBf16_, bool kFp8 = false>
 int launch(const LvsaAttnArgs* a, cudaStream_t stream, const LvsaFp8Scales* sc = nullptr) {
-  using L = Smem<D, STAGES, kFp8>;
+  using L = Smem<D, SK, SV, kFp8>;
   CUtensorMap mq, mk, mv, mtq, mtk, mtv;
   int st;
   const int dt = kFp8 ? LVSA_DTYPE_E4M3 : (kBf16_ ? LVSA_DTYPE_BF16 : LVSA_DTYPE_F16);
@@ -681,7 +683,7 @@ int launch(const LvsaAttnArgs* a, cudaStream_t stream, const LvsaFp8Scales* sc =
     p.vref = sc->v_ref;
   }
 
-  auto kern = lvsa_attn_kernel<D, STAGES, kBf16_, kFp8>;
+  auto kern = lvsa_attn_kernel<D, SK, SV, kBf16_, kFp8>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes) != cudaSuccess)
     return LVSA_ERR_CUDA;
   p.tok_off = a->token_offset;
@@ -732,12 +734,29 @@ extern "C" int lvsa_attn_fwd(const LvsaAttnArgs* a, void* stream) {
   const bool bf16 = a->dtype == LVSA_DTYPE_BF16;
   if (a->dtype != LVSA_DTYPE_BF16 && a->dtype != LVSA_DTYPE_F16) return LVSA_ERR_UNSUPPORTED;
   switch (a->head_dim) {
-    case 128: return bf16 ? launch<128, 3, true>(a, s) : launch<128, 3, false>(a, s);
-    case 64: return bf16 ? launch<64, 6, true>(a, s) : launch<64, 6, false>(a, s);
+// K and V ring depths (K stages free after their S MMA, V stages after their
+// PV MMA).  Measured on cfg2: 4 K + 2 V stages 32.07 ms/layer, 3 + 3 32.42,
+// 2 + 4 32.65, 5 + 1 47.8 -- K(j+2) is on the critical chain (S(j+2) is
+// issued right after PV(j)); D = 64 and FP8 (16 KB tiles): 6 + 6, within
+// noise of 8 + 5, 9 + 4 and 10 + 3.
+#ifndef LVSA_SK
+#define LVSA_SK 4
+#define LVSA_SV 2
+#endif
+#ifndef LVSA_SK64
+#define LVSA_SK64 6
+#define LVSA_SV64 6
+#endif
+    case 128: return bf16 ? launch<128, LVSA_SK, LVSA_SV, true>(a, s) : launch<128, LVSA_SK, LVSA_SV, false>(a, s);
+    case 64: return bf16 ? launch<64, LVSA_SK64, LVSA_SV64, true>(a, s) : launch<64, LVSA_SK64, LVSA_SV64, false>(a, s);
     default: return LVSA_ERR_UNSUPPORTED;
   }
 }
 
+#ifndef LVSA_SK8
+#define LVSA_SK8 6
+#define LVSA_SV8 6
+#endif
 extern "C" int lvsa_attn_fwd_fp8(const LvsaAttnArgs* a, const LvsaFp8Scales* sc, void* stream) {
   using namespace lvsa;
   const int v = validate(a);
@@ -746,7 +765,8 @@ extern "C" int lvsa_attn_fwd_fp8(const LvsaAttnArgs* a, const LvsaFp8Scales* sc,
   if (a->head_dim != 128) return LVSA_ERR_UNSUPPORTED;
   if (a->dtype != LVSA_DTYPE_BF16 && a->dtype != LVSA_DTYPE_F16) return LVSA_ERR_UNSUPPORTED;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  return a->dtype == LVSA_DTYPE_BF16 ? launch<128, 6, true, true>(a, s, sc) : launch<128, 6, false, true>(a, s, sc);
+  return a->dtype == LVSA_DTYPE_BF16 ? launch<128, LVSA_SK8, LVSA_SV8, true, true>(a, s, sc)
+                                      : launch<128, LVSA_SK8, LVSA_SV8, false, true>(a, s, sc);
 }
 
 extern "C" const char* lvsa_status_str(int status) {
