@@ -1,5 +1,10 @@
 // Block-sparse LVSA attention forward for sm_100a (tcgen05 + TMEM + TMA).
 //
+// Two kernels share the softmax and MMA code: lvsa_attn_kernel (one query
+// tile per CTA, described here; D = 64 and FP8) and lvsa_attn_pair_kernel
+// (two query tiles per CTA sharing their K/V loads; bf16/f16 D = 128),
+// described above its definition.
+//
 // One CTA per (128-row query tile, head, batch); 320 threads:
 //   warps 0-7  softmax, one thread per query row and key-tile class: warps
 //              0-3 take the even entries j of the row's tile list, warps 4-7
@@ -37,6 +42,7 @@
 #include <cuda_fp8.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdint>
 #include <cstring>
@@ -88,6 +94,9 @@ struct AttnParams {
   int nqt_all, nkt;  // query / key tiles of the text segment
   int tok_off;       // global token of the video segment's first token (sequence shards)
   int row0;          // first tile-CSR row of this launch
+  // Tile-pair kernel: video rows [row0, pair_ve) in pair_nv pairs, then text
+  // rows [pair_ts, pair_end).
+  int pair_ve, pair_ts, pair_end, pair_nv;
 };
 
 
@@ -588,6 +597,371 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ------------------------------------------------------------------ tile pairs
+// Two consecutive query tiles of one segment per CTA (same head, batch).
+// Class c (warps 4c .. 4c+3) owns query tile c of the pair with its own tile
+// list, S/P buffer, O accumulator and running max; nothing is merged.  Step i
+// of the CTA is entry i of both lists: when the two entries name the same key
+// tile (every step for two tiles of one frame) it is loaded once and read by
+// both classes' MMAs, which halves the L2 -> shared-memory traffic per
+// computed tile; otherwise each class's tile is loaded on its own.  The load
+// sequence (index g) is a function of the two lists, walked identically by
+// the producer and the MMA issuer.  MMA order: S_0(0) S_1(0), then per step i
+// PV_0(i) S_0(i+1) PV_1(i) S_1(i+1) -- the same two interleaved chains as the
+// single-tile kernel.
+template <int D, int SK, int SV, bool kFp8 = false>
+struct SmemPair {
+  static constexpr int kElem = kFp8 ? 1 : 2;
+  static constexpr int kCh = D * kElem / 128;
+  static constexpr int kTile = kCh * kChunk;
+  static constexpr int kQ = 0;  // two query tiles
+  static constexpr int kK = kQ + 2 * kTile;
+  static constexpr int kV = kK + SK * kTile;
+  static constexpr int kBar = kV + SV * kTile;
+  static constexpr int kNumBars = 2 * SK + 2 * SV + 8;
+  static constexpr int kMisc = kBar + kNumBars * 8;
+  static constexpr int kBytes = kMisc + 16 + 1024;
+  static_assert(kBytes <= 232448, "shared memory");
+};
+
+// Loads of step i: g0 / g1 = load index read by class 0 / 1 (-1: the class has
+// no entry i); shared when both read one load.
+struct PairStep {
+  int g0, g1;
+  bool shared;
+};
+__device__ __forceinline__ PairStep pair_step(int i, const int32_t* l0, int n0, const int32_t* l1, int n1, int& gc) {
+  PairStep s;
+  s.g0 = i < n0 ? gc++ : -1;
+  s.shared = i < n0 && i < n1 && l0[i] == l1[i];
+  s.g1 = i < n1 ? (s.shared ? s.g0 : gc++) : -1;
+  return s;
+}
+
+template <int D, int SK, int SV, bool kBf16, bool kFp8 = false>
+__global__ void __launch_bounds__(kThreads, 1)
+    lvsa_attn_pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                          const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_tq,
+                          const __grid_constant__ CUtensorMap tm_tk, const __grid_constant__ CUtensorMap tm_tv,
+                          const AttnParams prm) {
+  using L = SmemPair<D, SK, SV, kFp8>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem + L::kQ;
+  uint8_t* sK = smem + L::kK;
+  uint8_t* sV = smem + L::kV;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBar);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;
+  uint64_t* v_full = k_full + SK;
+  uint64_t* k_empty = v_full + SV;
+  uint64_t* v_empty = k_empty + SK;
+  uint64_t* s_full = v_empty + SV;  // [2] per class
+  uint64_t* p_full = s_full + 2;    // [2] per class
+  uint64_t* o_done = p_full + 2;
+  uint64_t* drain = o_done + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMisc);
+  volatile int* abort = reinterpret_cast<volatile int*>(smem + L::kMisc + 4);
+  volatile int* never = reinterpret_cast<volatile int*>(smem + L::kMisc + 8);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int h = blockIdx.y, b = blockIdx.z;
+  // Pairs of video rows [row0, pair_ve), then pairs of text rows [pair_ts, pair_end).
+  const int x = blockIdx.x;
+  const bool text_row = x >= prm.pair_nv;
+  const int row_a = text_row ? prm.pair_ts + 2 * (x - prm.pair_nv) : prm.row0 + 2 * x;
+  const bool has_b = row_a + 1 < (text_row ? prm.pair_end : prm.pair_ve);
+  const int beg0 = prm.indptr[row_a], n0 = prm.indptr[row_a + 1] - beg0;
+  const int beg1 = has_b ? prm.indptr[row_a + 1] : 0, n1 = has_b ? prm.indptr[row_a + 2] - beg1 : 0;
+  const int32_t* l0 = prm.indices + beg0;
+  const int32_t* l1 = prm.indices + beg1;
+  const int nmax = max(n0, n1);
+  const int tok_a = (text_row ? row_a - prm.nqv : row_a) * kBM;
+  const int hk = h / (prm.heads / prm.kv_heads);
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < SK; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+    }
+    for (int s = 0; s < SV; ++s) {
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 128);
+    }
+    mbar_init(o_done, 1);
+    mbar_init(drain, 1);
+    *abort = 0;
+    *never = 0;
+    fence_mbar_init();
+  }
+  if (warp == kMmaWarp) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS = tmem, tO = tmem + 256;
+
+  if (warp == kProducerWarp) {
+    // ---------------------------------------------------------- producer
+    if (lane == 0 && nmax > 0) {
+      const CUtensorMap* mq = text_row ? &tm_tq : &tm_q;
+      tma_prefetch_desc(mq);
+      tma_prefetch_desc(&tm_k);
+      tma_prefetch_desc(&tm_v);
+      mbar_expect_tx(q_full, (has_b ? 2 : 1) * L::kTile);
+      for (int t = 0; t < (has_b ? 2 : 1); ++t)
+#pragma unroll
+        for (int c = 0; c < L::kCh; ++c)
+          tma_load_4d(sQ + t * L::kTile + c * kChunk, mq, q_full, c * (128 / L::kElem), h, tok_a + t * kBM, b);
+      int gc = 0, issued = 0;
+      bool ok = true;
+      for (int i = 0; ok && i < nmax; ++i) {
+        const PairStep st = pair_step(i, l0, n0, l1, n1, gc);
+        for (int t = 0; t < 2; ++t) {
+          const int g = t == 0 ? st.g0 : (st.shared ? -1 : st.g1);
+          if (g < 0) continue;
+          const int kt = t == 0 ? l0[i] : l1[i];
+          const int s = g % SK, sv = g % SV;
+          const bool tt = kt >= prm.nkv;
+          const int ktok = (tt ? kt - prm.nkv : kt) * kBN;
+          const CUtensorMap* mk = tt ? &tm_tk : &tm_k;
+          const CUtensorMap* mv = tt ? &tm_tv : &tm_v;
+          if (g >= SK && !(ok = mbar_wait(&k_empty[s], ((g / SK) - 1) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT)))
+            break;
+          mbar_expect_tx(&k_full[s], L::kTile);
+#pragma unroll
+          for (int c = 0; c < L::kCh; ++c)
+            tma_load_4d(sK + s * L::kTile + c * kChunk, mk, &k_full[s], c * (128 / L::kElem), hk, ktok, b);
+          if (g >= SV && !(ok = mbar_wait(&v_empty[sv], ((g / SV) - 1) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT))) {
+            issued = -(g + 1);  // K of load g issued, V not
+            break;
+          }
+          mbar_expect_tx(&v_full[sv], L::kTile);
+#pragma unroll
+          for (int c = 0; c < L::kCh; ++c)
+            tma_load_4d(sV + sv * L::kTile + c * kChunk, mv, &v_full[sv], c * (128 / L::kElem), hk, ktok, b);
+          issued = g + 1;
+        }
+      }
+      if (*abort) {
+        // Drain our own copies still in flight before the CTA retires.
+        const int k_issued = issued < 0 ? -issued : issued, v_issued = issued < 0 ? -issued - 1 : issued;
+        mbar_wait(q_full, 0, never, nullptr, 0);
+        for (int g = max(0, k_issued - SK); g < k_issued; ++g)
+          mbar_wait(&k_full[g % SK], (g / SK) & 1, never, nullptr, 0);
+        for (int g = max(0, v_issued - SV); g < v_issued; ++g)
+          mbar_wait(&v_full[g % SV], (g / SV) & 1, never, nullptr, 0);
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    // ---------------------------------------------------------- MMA issuer
+    if (lane == 0 && nmax > 0) {
+      constexpr bool kFmt1 = kBf16 && !kFp8;
+      constexpr uint32_t idS = idesc_f16(kBM, kBN, kFmt1, false);
+      constexpr uint32_t idO = idesc_f16(kBM, D, kFmt1, true);
+      const uint32_t q_base = smem_u32(sQ), k_base = smem_u32(sK), v_base = smem_u32(sV);
+      const int nc[2] = {n0, n1};
+      // S_c(i) from load g; `last`: no later S reads that K stage.
+      auto issue_s = [&](int c, int g, bool last) -> bool {
+        if (!mbar_wait(&k_full[g % SK], (g / SK) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT)) return false;
+        tc_fence_after();
+        const uint32_t kb = k_base + (g % SK) * L::kTile, qb = q_base + c * L::kTile, dS = tS + c * 128;
+#pragma unroll
+        for (int kk = 0; kk < D * L::kElem / 32; ++kk) {
+          const uint32_t off = (kk >> 2) * kChunk + (kk & 3) * 32;
+          mma_ss_any<kFp8>(dS, sdesc_sw128(qb + off, 16, 1024), sdesc_sw128(kb + off, 16, 1024), idS, kk > 0);
+        }
+        mma_commit(&s_full[c]);
+        if (last) mma_commit(&k_empty[g % SK]);
+        return true;
+      };
+      auto issue_pv = [&](int c, int i, int g, bool last) -> bool {
+        if (!mbar_wait(&p_full[c], i & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT)) return false;
+        if (!mbar_wait(&v_full[g % SV], (g / SV) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT)) return false;
+        tc_fence_after();
+        const uint32_t vb = v_base + (g % SV) * L::kTile, pa = tS + c * 128, dO = tO + c * 128;
+#pragma unroll
+        for (int kk = 0; kk < kBN * L::kElem / 32; ++kk)
+          mma_ts_any<kFp8>(dO, pa + kk * 8, sdesc_sw128(vb + kk * (32 / L::kElem) * 128, kChunk, 1024), idO,
+                           (i > 0 || kk > 0));
+        if (last) mma_commit(&v_empty[g % SV]);
+        return true;
+      };
+      bool ok = mbar_wait(q_full, 0, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT);
+      int gc = 0;
+      PairStep cur = pair_step(0, l0, n0, l1, n1, gc);
+      if (ok && cur.g0 >= 0) ok = issue_s(0, cur.g0, !cur.shared);
+      if (ok && cur.g1 >= 0) ok = issue_s(1, cur.g1, true);
+      for (int i = 0; ok && i < nmax; ++i) {
+        PairStep nxt = {-1, -1, false};
+        if (i + 1 < nmax) nxt = pair_step(i + 1, l0, n0, l1, n1, gc);
+        for (int c = 0; ok && c < 2; ++c) {
+          if (i >= nc[c]) continue;
+          // PV_c(i); class 0 leaves a shared V stage to class 1.
+          ok = issue_pv(c, i, c == 0 ? cur.g0 : cur.g1, c == 1 || !cur.shared);
+          // S_c(i+1) reuses buffer c: P_c(i) was read by PV_c(i), issued just before.
+          if (ok && i + 1 < nc[c]) ok = issue_s(c, c == 0 ? nxt.g0 : nxt.g1, c == 1 || !nxt.shared);
+        }
+        cur = nxt;
+      }
+      if (ok) mma_commit(o_done);
+      mma_commit(drain);
+      mbar_wait(drain, 0, never, nullptr, 0);
+    }
+  } else {
+    // ---------------------------------------------------------- softmax
+    const int cls = warp >> 2;                // query tile of the pair
+    const int r = ((warp & 3) << 5) | lane;   // query row = TMEM lane
+    const int row = row_a + cls;
+    const int beg = cls ? beg1 : beg0, n = cls ? n1 : n0;
+    const bool mine = cls == 0 || has_b;
+    const int seg_len = text_row ? prm.n_text : prm.n_video;
+    const int tok = tok_a + cls * kBM + r;
+    const bool valid = mine && tok < seg_len;
+    const int fq = text_row ? 0 : min((prm.tok_off + tok) / prm.P, prm.T - 1);
+    const uint32_t* fbits = prm.frame_bits + static_cast<size_t>(fq) * prm.words;
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t tSc = tS + cls * 128 + lane_base;
+    const uint32_t tOc = tO + cls * 128 + lane_base;
+    const float sl2_base = prm.scale_log2;
+    float sq = 1.f, vref = 1.f;
+    if constexpr (kFp8) {
+      if (mine) {
+        sq = text_row ? prm.tqs[(static_cast<int64_t>(b) * prm.heads + h) * prm.nqt_all + (row - prm.nqv)]
+                      : prm.qs[(static_cast<int64_t>(b) * prm.heads + h) * prm.nqv + row];
+        vref = prm.vref[static_cast<int64_t>(b) * prm.kv_heads + hk];
+      }
+    }
+    constexpr int kPHalf = kFp8 ? 16 : 32;
+    float m = kNegInf, l = 0.f;
+    bool ok = true;
+    int flag_next = n > 0 ? prm.flags[beg] : 0;
+    int kt_next = n > 0 ? prm.indices[beg] : 0;
+    for (int it = 0; it < n; ++it) {
+      const int flag = flag_next, kt = kt_next;
+      if (it + 1 < n) {
+        flag_next = prm.flags[beg + it + 1];
+        kt_next = prm.indices[beg + it + 1];
+      }
+      float sl2 = sl2_base, pscale = 1.f;
+      if constexpr (kFp8) {
+        const int64_t hb = static_cast<int64_t>(b) * prm.kv_heads + hk;
+        const bool tt = kt >= prm.nkv;
+        const float skj = tt ? prm.tks[hb * prm.nkt + (kt - prm.nkv)] : prm.ks[hb * prm.nkv + kt];
+        const float svj = tt ? prm.tvs[hb * prm.nkt + (kt - prm.nkv)] : prm.vs[hb * prm.nkv + kt];
+        sl2 = sl2_base * sq * skj;
+        pscale = svj / vref;
+      }
+      uint32_t am[4] = {~0u, ~0u, ~0u, ~0u};
+      if (flag) tile_mask(am, prm, kt, text_row, fbits);
+      if (!__all_sync(0xFFFFFFFFu, mbar_wait(&s_full[cls], it & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t sv[64];
+      float mx_hi;
+      {
+        uint32_t hv[64];
+        tmem_ld64x2(tSc, tSc + 64, sv, hv);
+        if (flag) mask64(hv, am[2], am[3]);
+        mx_hi = max64(hv);
+      }
+      if (flag) mask64(sv, am[0], am[1]);
+      const float m_new = fmaxf(m, fmaxf(max64(sv), mx_hi) * sl2);
+      if (it == 0) {
+        m = m_new;
+      } else {
+        // Lazy rescale of my O buffer: PV_c(it-1) was issued before S_c(it).
+        const bool need = m_new > m + kRescaleThreshold;
+        if (__any_sync(0xFFFFFFFFu, need)) {
+          const float alpha = need ? ex2_approx(m - m_new) : 1.f;
+          if (need) m = m_new;
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t t[32];
+            tmem_ld32(tOc + c * 32, t);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) t[i] = __float_as_uint(__uint_as_float(t[i]) * alpha);
+            tmem_st32(tOc + c * 32, t);
+          }
+          l *= alpha;
+        }
+      }
+      const float mu = (m == kNegInf) ? 0.f : m;
+      const uint64_t sl2x2 = f2_pack(sl2, sl2), nmu2 = f2_pack(-mu, -mu);
+      uint32_t pk[32];
+      l += exp64<kBf16, kFp8>(sv, sl2x2, nmu2, pscale, pk);
+      store_p<kFp8>(tSc, pk);
+      tmem_ld64(tSc + 64, sv);
+      if (flag) mask64(sv, am[2], am[3]);
+      l += exp64<kBf16, kFp8>(sv, sl2x2, nmu2, pscale, pk);
+      store_p<kFp8>(tSc + kPHalf, pk);
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&p_full[cls]);
+    }
+    // ---------------------------------------------------------- epilogue
+    using Elem = typename std::conditional<kBf16, __nv_bfloat16, __half>::type;
+    Elem* obase = nullptr;
+    float* lse = nullptr;
+    if (text_row) {
+      if (prm.text_o)
+        obase = reinterpret_cast<Elem*>(prm.text_o) + b * prm.to_sb + static_cast<int64_t>(tok) * prm.to_st +
+                h * prm.to_sh;
+      if (prm.text_lse) lse = prm.text_lse + (static_cast<int64_t>(b) * prm.heads + h) * prm.n_text + tok;
+    } else {
+      obase = reinterpret_cast<Elem*>(prm.o) + b * prm.o_sb + static_cast<int64_t>(tok) * prm.o_st + h * prm.o_sh;
+      if (prm.lse) lse = prm.lse + (static_cast<int64_t>(b) * prm.heads + h) * prm.n_video + tok;
+    }
+    if (n > 0) {
+      const bool got =
+          ok && __all_sync(0xFFFFFFFFu, mbar_wait(o_done, 0, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT));
+      if (got) {
+        tc_fence_after();
+        const float inv = (l > 0.f) ? vref / l : 0.f;
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t t[32];
+          tmem_ld32(tOc + c * 32, t);
+          if (valid && obase) {
+            uint32_t pk[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              pk[i] = pack2(__uint_as_float(t[2 * i]) * inv, __uint_as_float(t[2 * i + 1]) * inv, kBf16);
+            uint4* dst = reinterpret_cast<uint4*>(obase + c * 32);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+          }
+        }
+        if (valid && lse) *lse = (l > 0.f) ? (m + __log2f(l)) * 0.69314718055994531f : kNegInf;
+      }
+    } else if (valid) {
+      if (obase) {
+        uint4* dst = reinterpret_cast<uint4*>(obase);
+#pragma unroll
+        for (int i = 0; i < D / 8; ++i) dst[i] = make_uint4(0u, 0u, 0u, 0u);
+      }
+      if (lse) *lse = kNegInf;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
 // ------------------------------------------------------------------ host side
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -633,9 +1007,8 @@ int make_map(CUtensorMap* map, const LvsaTensor& t, int B, int N, int Hx, int D,
   return r == CUDA_SUCCESS ? LVSA_OK : LVSA_ERR_ALIGNMENT;
 }
 
-template <int D, int SK, int SV, bool kBf16_, bool kFp8 = false>
+template <int D, int SK, int SV, bool kBf16_, bool kFp8 = false, bool kPair = false>
 int launch(const LvsaAttnArgs* a, cudaStream_t stream, const LvsaFp8Scales* sc = nullptr) {
-  using L = Smem<D, SK, SV, kFp8>;
   CUtensorMap mq, mk, mv, mtq, mtk, mtv;
   int st;
   const int dt = kFp8 ? LVSA_DTYPE_E4M3 : (kBf16_ ? LVSA_DTYPE_BF16 : LVSA_DTYPE_F16);
@@ -683,15 +1056,31 @@ int launch(const LvsaAttnArgs* a, cudaStream_t stream, const LvsaFp8Scales* sc =
     p.vref = sc->v_ref;
   }
 
-  auto kern = lvsa_attn_kernel<D, SK, SV, kBf16_, kFp8>;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes) != cudaSuccess)
-    return LVSA_ERR_CUDA;
   p.tok_off = a->token_offset;
   p.row0 = a->first_q_tile;
-  const int rows = (text_rows ? a->n_q_tiles : a->n_q_video_tiles) - a->first_q_tile;
+  const int end = text_rows ? a->n_q_tiles : a->n_q_video_tiles;
+  const int rows = end - a->first_q_tile;
   if (rows <= 0) return LVSA_OK;
-  dim3 grid(rows, a->heads, a->batch);
-  kern<<<grid, kThreads, L::kBytes, stream>>>(mq, mk, mv, mtq, mtk, mtv, p);
+  p.pair_end = end;
+  p.pair_ve = std::min(end, a->n_q_video_tiles);
+  p.pair_ts = std::max(a->first_q_tile, a->n_q_video_tiles);
+  p.pair_nv = p.pair_ve > p.row0 ? (p.pair_ve - p.row0 + 1) / 2 : 0;
+  if constexpr (kPair) {
+    using L = SmemPair<D, SK, SV, kFp8>;
+    auto kern = lvsa_attn_pair_kernel<D, SK, SV, kBf16_, kFp8>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes) != cudaSuccess)
+      return LVSA_ERR_CUDA;
+    const int pair_nt = end > p.pair_ts ? (end - p.pair_ts + 1) / 2 : 0;
+    dim3 grid(p.pair_nv + pair_nt, a->heads, a->batch);
+    kern<<<grid, kThreads, L::kBytes, stream>>>(mq, mk, mv, mtq, mtk, mtv, p);
+  } else {
+    using L = Smem<D, SK, SV, kFp8>;
+    auto kern = lvsa_attn_kernel<D, SK, SV, kBf16_, kFp8>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes) != cudaSuccess)
+      return LVSA_ERR_CUDA;
+    dim3 grid(rows, a->heads, a->batch);
+    kern<<<grid, kThreads, L::kBytes, stream>>>(mq, mk, mv, mtq, mtk, mtv, p);
+  }
   return cudaGetLastError() == cudaSuccess ? LVSA_OK : LVSA_ERR_CUDA;
 }
 
@@ -734,11 +1123,17 @@ extern "C" int lvsa_attn_fwd(const LvsaAttnArgs* a, void* stream) {
   const bool bf16 = a->dtype == LVSA_DTYPE_BF16;
   if (a->dtype != LVSA_DTYPE_BF16 && a->dtype != LVSA_DTYPE_F16) return LVSA_ERR_UNSUPPORTED;
   switch (a->head_dim) {
-// K and V ring depths (K stages free after their S MMA, V stages after their
-// PV MMA).  Measured on cfg2: 4 K + 2 V stages 32.07 ms/layer, 3 + 3 32.42,
-// 2 + 4 32.65, 5 + 1 47.8 -- K(j+2) is on the critical chain (S(j+2) is
-// issued right after PV(j)); D = 64 and FP8 (16 KB tiles): 6 + 6, within
-// noise of 8 + 5, 9 + 4 and 10 + 3.
+// Kernel choice and K / V ring depths (K stages free after their S MMA, V
+// stages after their PV MMA), measured in a 10-launch loop:
+//  * D = 128, bf16/f16: the tile-pair kernel with 3 K + 2 V stages, 32.25
+//    ms/layer on cfg2 against 32.61-32.73 for the single-tile kernel on the
+//    same GPU (2 + 2: 32.39, 2 + 3: 32.34).  Single-tile ring: 4 K + 2 V
+//    stages 32.07 (another GPU), 3 + 3 32.42, 2 + 4 32.65, 5 + 1 47.8 --
+//    K(j+2) is on its critical chain (S(j+2) is issued right after PV(j)).
+//  * D = 64 and FP8 (16 KB tiles): the single-tile kernel with 6 + 6 stages
+//    (within noise of 8 + 5, 9 + 4 and 10 + 3).  The tile-pair kernel was
+//    slower there: cfg5 37.84-38.12 vs 37.28, FP8 cfg2 28.87-29.02 vs 27.86
+//    (LVSA_PAIR64 / LVSA_PAIR8 = 1 select it).
 #ifndef LVSA_SK
 #define LVSA_SK 4
 #define LVSA_SV 2
@@ -747,8 +1142,28 @@ extern "C" int lvsa_attn_fwd(const LvsaAttnArgs* a, void* stream) {
 #define LVSA_SK64 6
 #define LVSA_SV64 6
 #endif
+#ifndef LVSA_PAIR
+#define LVSA_PAIR 1
+#define LVSA_SKP 3
+#define LVSA_SVP 2
+#endif
+#if LVSA_PAIR
+    case 128: return bf16 ? launch<128, LVSA_SKP, LVSA_SVP, true, false, true>(a, s)
+                          : launch<128, LVSA_SKP, LVSA_SVP, false, false, true>(a, s);
+#else
     case 128: return bf16 ? launch<128, LVSA_SK, LVSA_SV, true>(a, s) : launch<128, LVSA_SK, LVSA_SV, false>(a, s);
+#endif
+#ifndef LVSA_PAIR64
+#define LVSA_PAIR64 0
+#define LVSA_SKP64 6
+#define LVSA_SVP64 6
+#endif
+#if LVSA_PAIR64
+    case 64: return bf16 ? launch<64, LVSA_SKP64, LVSA_SVP64, true, false, true>(a, s)
+                         : launch<64, LVSA_SKP64, LVSA_SVP64, false, false, true>(a, s);
+#else
     case 64: return bf16 ? launch<64, LVSA_SK64, LVSA_SV64, true>(a, s) : launch<64, LVSA_SK64, LVSA_SV64, false>(a, s);
+#endif
     default: return LVSA_ERR_UNSUPPORTED;
   }
 }
@@ -765,8 +1180,18 @@ extern "C" int lvsa_attn_fwd_fp8(const LvsaAttnArgs* a, const LvsaFp8Scales* sc,
   if (a->head_dim != 128) return LVSA_ERR_UNSUPPORTED;
   if (a->dtype != LVSA_DTYPE_BF16 && a->dtype != LVSA_DTYPE_F16) return LVSA_ERR_UNSUPPORTED;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+#ifndef LVSA_PAIR8
+#define LVSA_PAIR8 0
+#define LVSA_SKP8 6
+#define LVSA_SVP8 6
+#endif
+#if LVSA_PAIR8
+  return a->dtype == LVSA_DTYPE_BF16 ? launch<128, LVSA_SKP8, LVSA_SVP8, true, true, true>(a, s, sc)
+                                      : launch<128, LVSA_SKP8, LVSA_SVP8, false, true, true>(a, s, sc);
+#else
   return a->dtype == LVSA_DTYPE_BF16 ? launch<128, LVSA_SK8, LVSA_SV8, true, true>(a, s, sc)
                                       : launch<128, LVSA_SK8, LVSA_SV8, false, true>(a, s, sc);
+#endif
 }
 
 extern "C" const char* lvsa_status_str(int status) {
