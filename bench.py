@@ -43,8 +43,8 @@ CONFIGS = {
 METRIC = "sparse-attn ms/layer & useful TFLOPS (% of B200 peak) at 1/2/4/8 GPUs"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 # DRAM bytes (read + write) per attention launch, from one ncu capture of a
-# full-size layer (profiles/lvsa_attn_cfg2_full.md); null where not captured.
-NCU_TRAFFIC_BYTES = {"cfg2": 1.586e9}
+# full-size layer (profiles/lvsa_attn_pair_cfg2_full.md); null where not captured.
+NCU_TRAFFIC_BYTES = {"cfg2": 1.602e9}
 
 
 def log(*a):
