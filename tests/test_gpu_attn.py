@@ -146,3 +146,45 @@ def test_attention_baseline_configs_sampled(cfg):
     assert (o1.float() - 1).abs().max().item() <= 1e-2, "V == 1 must give 1 (coverage / normalisation)"
     if nt:
         assert (t1.float() - 1).abs().max().item() <= 1e-2
+
+
+@pytest.mark.parametrize("D,fp8", [(128, False), (64, False), (128, True)])
+def test_attention_arbitrary_tile_lists(D, fp8):
+    """Hand-made tile CSR (no in-tile masks): adjacent query tiles with equal,
+    nested, disjoint, reordered and empty key-tile lists, and an odd number of
+    query tiles.  Exercises every branch of the tile-pair kernel's shared load
+    sequence (bf16 D=128) and the single-tile kernel (D=64, FP8)."""
+    import dataclasses
+    from longvideosparseattention_b200 import block_sparse_attention, build_block_mask, check_device_errors
+    T, P, H, B = 9, 128, 2, 1          # 9 query tiles of 128 tokens, 9 key tiles
+    n = T * P
+    lists = [
+        [0, 1, 2], [0, 1, 2],          # equal
+        [3, 4], [3, 4, 5, 6],          # prefix / superset
+        [8, 0], [1, 7],                # disjoint, unsorted
+        [], [2, 5, 8, 1, 0, 3, 4],     # empty row next to a long one
+        [6, 2, 4],                     # last tile, no partner
+    ]
+    m = build_block_mask(T, P, 1, 1, None, 0, True, 0, device="cuda")
+    indptr = np.zeros(len(lists) + 1, np.int32)
+    indptr[1:] = np.cumsum([len(x) for x in lists])
+    idx = np.array([t for x in lists for t in x], np.int32)
+    m = dataclasses.replace(
+        m, tile_indptr=torch.from_numpy(indptr).cuda(), tile_indices=torch.from_numpy(idx).cuda(),
+        tile_flags=torch.zeros(len(idx), dtype=torch.uint8, device="cuda"))
+    q = seeded((B, n, H, D), 11)
+    k = seeded((B, n, H, D), 12)
+    v = seeded((B, n, H, D), 13)
+    out, _ = block_sparse_attention(q, k, v, m, fp8=fp8)
+    torch.cuda.synchronize()
+    check_device_errors(q.device)
+    qf, kf, vf = (x.float().cpu()[0] for x in (q, k, v))       # [n, H, D]
+    want = torch.zeros(n, H, D)
+    for r, tiles in enumerate(lists):
+        if not tiles:
+            continue
+        keys = torch.cat([torch.arange(t * P, (t + 1) * P) for t in tiles])
+        s = torch.einsum("qhd,khd->hqk", qf[r * P:(r + 1) * P], kf[keys]) / D ** 0.5
+        want[r * P:(r + 1) * P] = torch.einsum("hqk,khd->qhd", torch.softmax(s, -1), vf[keys])
+    tol = dict(max_abs=6e-2, mean_abs=6e-3) if fp8 else {}
+    assert_close(to_np(out)[0], want.numpy(), what=f"D={D} fp8={fp8}", **tol)
