@@ -43,7 +43,7 @@ CONFIGS = {
 METRIC = "sparse-attn ms/layer & useful TFLOPS (% of B200 peak) at 1/2/4/8 GPUs"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 # DRAM bytes (read + write) per attention launch, from one ncu capture of a
-# full-size layer (profiles/lvsa_attn_pair_cfg2_full.md); null where not captured.
+# full-size layer (dram__bytes_read.sum + dram__bytes_write.sum); null where not captured.
 NCU_TRAFFIC_BYTES = {"cfg2": 1.602e9}
 
 
@@ -239,7 +239,7 @@ def run_b200(args, cfg):
     def step(s, ev=None):
         nonlocal mask
         mask = build_block_mask(T, P, cfg["W"], cfg["n_first"], cfg["kfi"],
-                                (cfg["step"] + s * 0) % cfg["kfi"], True, nt, device=dev, reuse=mask)
+                                cfg["step"] % cfg["kfi"], True, nt, device=dev, reuse=mask)
         for i, lay in enumerate(layers):
             if ev is not None:
                 ev[i][0].record(stream)

@@ -26,7 +26,9 @@ enum {
   LVSA_ERR_GEOMETRY = 2,     /* pattern/sequence geometry inconsistent           */
   LVSA_ERR_UNSUPPORTED = 3,  /* head_dim / dtype / block size not built          */
   LVSA_ERR_ALIGNMENT = 4,    /* pointer or stride violates the 16-byte TMA rule  */
-  LVSA_ERR_CAPACITY = 5,     /* caller buffer smaller than lvsa_mask_layout says */
+  LVSA_ERR_CAPACITY = 5,     /* a buffer is too small: the caller's (vs
+                                lvsa_mask_layout) or the library's fixed
+                                no-allocation scratch                          */
   LVSA_ERR_CUDA = 6,         /* a CUDA runtime call failed                       */
   LVSA_ERR_DEVICE_TIMEOUT = 7 /* a kernel's bounded wait expired (error word)    */
 };
@@ -223,8 +225,12 @@ int lvsa_qk_prologue(const LvsaQkPrologue* args, void* stream);
  *    tile and head of each, and one fp32 per batch and K/V head, each part
  *    rounded up to 256 bytes; a larger call returns LVSA_ERR_CAPACITY and
  *    launches nothing.
- *  - The first call on a device looks up the array's device address with
- *    that device current; make that first call before any stream capture.
+ *  - The first call in each CUDA context (normally a device's primary
+ *    context) looks up the array's device address with that context
+ *    current; make that first call before any stream capture.
+ *  - Every argument check runs before anything is cleared or launched: a
+ *    rejected call (bad geometry, null pointers, over capacity) leaves the
+ *    scratch array and the stream untouched.
  *  - All calls share the one array and it keeps the previous call's
  *    contents; the part that must start at zero (the per-head V reference)
  *    is cleared by each call.  Calls that overlap on the GPU (different

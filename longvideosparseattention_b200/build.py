@@ -2,10 +2,14 @@
 
 ``python -m longvideosparseattention_b200.build`` (or ``__graft_entry__.build()``)
 runs nvcc on ``csrc/*.cu`` and writes the shared library next to this file, so
-it travels with the source tree.  Rebuilds only when a source is newer.
+it travels with the source tree.  A stamp file beside the library holds a
+SHA-256 of every source, header and nvcc flag it was built from; the library
+is rebuilt whenever that digest differs (never trusted by modification time,
+since the library is shipped alongside the sources and its mtime says nothing).
 """
 
 import glob
+import hashlib
 import os
 import subprocess
 import sys
@@ -13,6 +17,7 @@ import sys
 PKG = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(PKG)
 LIB = os.path.join(PKG, "liblvsa_b200.so")
+STAMP = LIB + ".sha256"
 NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",
               "-shared", "-Xcompiler", "-fPIC", "-Xptxas", "-v", "--expt-relaxed-constexpr"]
 
@@ -26,11 +31,21 @@ def _deps():
         sorted(glob.glob(os.path.join(ROOT, "include", "*.h")))
 
 
+def source_digest() -> str:
+    h = hashlib.sha256()
+    h.update(" ".join(NVCC_FLAGS).encode())
+    for p in _deps():
+        h.update(os.path.relpath(p, ROOT).encode())
+        with open(p, "rb") as fh:
+            h.update(fh.read())
+    return h.hexdigest()
+
+
 def up_to_date() -> bool:
-    if not os.path.exists(LIB):
+    if not (os.path.exists(LIB) and os.path.exists(STAMP)):
         return False
-    t = os.path.getmtime(LIB)
-    return all(os.path.getmtime(p) <= t for p in _deps())
+    with open(STAMP) as fh:
+        return fh.read().strip() == source_digest()
 
 
 def build(force: bool = False, verbose: bool = False) -> str:
@@ -42,6 +57,8 @@ def build(force: bool = False, verbose: bool = False) -> str:
     if r.returncode != 0:
         raise RuntimeError("nvcc failed:\n" + r.stdout + r.stderr)
     os.replace(LIB + ".tmp", LIB)
+    with open(STAMP, "w") as fh:
+        fh.write(source_digest() + "\n")
     if verbose:
         print(r.stderr)
     return LIB

@@ -1113,6 +1113,10 @@ int validate(const LvsaAttnArgs* a) {
   return LVSA_OK;
 }
 }  // namespace
+
+// The argument and geometry checks of lvsa_attn_fwd / lvsa_attn_fwd_fp8, for
+// entry points that must reject a call before they launch anything.
+int validate_attn_args(const LvsaAttnArgs* a) { return validate(a); }
 }  // namespace lvsa
 
 extern "C" int lvsa_attn_fwd(const LvsaAttnArgs* a, void* stream) {

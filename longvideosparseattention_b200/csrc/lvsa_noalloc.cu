@@ -5,6 +5,7 @@
 // tile scales and the per-head V reference go to one file-scope device array
 // instead of memory allocated per call.  Capacity and concurrency rules are
 // stated beside the declaration of lvsa_attn_fwd_fp8_noalloc in lvsa_b200.h.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -17,22 +18,59 @@ namespace {
 // Held by every GPU that loads the library, until the process exits.
 static __device__ __align__(256) uint8_t g_noalloc_scratch[LVSA_NOALLOC_SCRATCH_BYTES];
 
-constexpr int kMaxDevices = 64;
-uint8_t* g_scratch_addr[kMaxDevices] = {};
+// The device address of g_noalloc_scratch, per CUDA context (the array is
+// instantiated once per context that loads this module, so an address found
+// in one context is not valid in another, even on the same device).
+struct ScratchSlot {
+  CUcontext ctx;
+  uint8_t* addr;
+};
+constexpr int kMaxContexts = 64;
+ScratchSlot g_slots[kMaxContexts] = {};
+int g_n_slots = 0;
 std::mutex g_setup_mutex;
 
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+
+CtxGetCurrentFn ctx_get_current() {
+  static CtxGetCurrentFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetCurrentFn>(p);
+  });
+  return fn;
+}
+
 // In host code g_noalloc_scratch names a host-side stand-in; the device
-// address is looked up once per device, with that device current.
+// address is looked up once per context, with that context current.
 int scratch_address(uint8_t** out) {
   int dev = -1;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return LVSA_ERR_CUDA;
-  std::lock_guard<std::mutex> lock(g_setup_mutex);
-  if (!g_scratch_addr[dev]) {
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) return LVSA_ERR_CUDA;
+  CtxGetCurrentFn get = ctx_get_current();
+  CUcontext ctx = nullptr;
+  if (!get || get(&ctx) != CUDA_SUCCESS) return LVSA_ERR_CUDA;
+  if (!ctx) {
+    // No context current yet: the runtime call makes the device's primary
+    // context current as a side effect.
     void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) return LVSA_ERR_CUDA;
-    g_scratch_addr[dev] = static_cast<uint8_t*>(p);
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || get(&ctx) != CUDA_SUCCESS || !ctx)
+      return LVSA_ERR_CUDA;
   }
-  *out = g_scratch_addr[dev];
+  std::lock_guard<std::mutex> lock(g_setup_mutex);
+  for (int i = 0; i < g_n_slots; ++i)
+    if (g_slots[i].ctx == ctx) {
+      *out = g_slots[i].addr;
+      return LVSA_OK;
+    }
+  if (g_n_slots == kMaxContexts) return LVSA_ERR_CAPACITY;
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) return LVSA_ERR_CUDA;
+  g_slots[g_n_slots++] = ScratchSlot{ctx, static_cast<uint8_t*>(p)};
+  *out = static_cast<uint8_t*>(p);
   return LVSA_OK;
 }
 
@@ -40,12 +78,17 @@ size_t round256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
 }  // namespace
 
+namespace lvsa {
+int validate_attn_args(const LvsaAttnArgs* a);
+}
+
 extern "C" int lvsa_attn_fwd_fp8_noalloc(const LvsaAttnArgs* a, void* stream) {
-  if (!a || !a->q.ptr || !a->k.ptr || !a->v.ptr) return LVSA_ERR_INVALID_ARG;
+  // Every check lvsa_attn_fwd_fp8 makes, before anything is cleared or
+  // launched: a rejected call leaves the scratch array and the GPU untouched.
+  int st = lvsa::validate_attn_args(a);
+  if (st != LVSA_OK) return st;
   if (a->dtype != LVSA_DTYPE_BF16 && a->dtype != LVSA_DTYPE_F16) return LVSA_ERR_UNSUPPORTED;
   if (a->head_dim != 128) return LVSA_ERR_UNSUPPORTED;
-  if (a->batch < 1 || a->n_video < 1 || a->n_text < 0 || a->heads < 1 || a->kv_heads < 1)
-    return LVSA_ERR_INVALID_ARG;
   const bool has_text = a->n_text > 0;
   const bool text_rows = has_text && a->text_q.ptr != nullptr;
   if (has_text && (!a->text_k.ptr || !a->text_v.ptr)) return LVSA_ERR_INVALID_ARG;
@@ -71,7 +114,7 @@ extern "C" int lvsa_attn_fwd_fp8_noalloc(const LvsaAttnArgs* a, void* stream) {
   if (off > LVSA_NOALLOC_SCRATCH_BYTES) return LVSA_ERR_CAPACITY;
 
   uint8_t* base = nullptr;
-  int st = scratch_address(&base);
+  st = scratch_address(&base);
   if (st != LVSA_OK) return st;
   auto f32 = [base](size_t at) { return reinterpret_cast<float*>(base + at); };
   // The V reference is a running atomic max over this call's tiles: clear it.

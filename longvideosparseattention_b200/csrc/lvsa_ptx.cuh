@@ -244,28 +244,6 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
-// 2^x evaluated on the FMA/ALU pipes instead of the MUFU unit, for the
-// softmax arguments x <= ~8.  Range reduction: j = round(x) by adding
-// 1.5 * 2^23 (fp32 round-to-nearest leaves j in the low mantissa bits),
-// f = x - j in [-0.5, 0.5]; 2^f by a degree-3 polynomial whose coefficients
-// were fitted here for minimax relative error on [-0.5, 0.5] with Lawson's
-// iteratively reweighted least squares (max relative error 7.5e-5, far below
-// the 2^-9 of the bf16 P it feeds); 2^j is added into the exponent field.
-// x below -126 (including -inf from the mask) returns exactly 0.
-__device__ __forceinline__ float ex2_poly(float x) {
-  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
-  constexpr int kRoundBits = 0x4B400000;
-  const float xc = fmaxf(x, -126.0f);
-  const float t = xc + kRound;
-  const float f = xc - (t - kRound);
-  float p = fmaf(0.05517167f, f, 0.24261114f);
-  p = fmaf(p, f, 0.69326099f);
-  p = fmaf(p, f, 0.99992807f);
-  const int j = __float_as_int(t) - kRoundBits;
-  const float y = __int_as_float(__float_as_int(p) + (j << 23));
-  return x < -126.0f ? 0.0f : y;
-}
-
 // ---------------------------------------------------------------- f32x2
 // Blackwell packed-fp32 arithmetic: one instruction on two lanes of a
 // 64-bit register pair.
@@ -286,30 +264,6 @@ __device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
   uint64_t d;
   asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
-}
-
-// ex2_poly on two lanes at once (same method and coefficients), using the
-// packed FMA/add for the arithmetic part.
-__device__ __forceinline__ void ex2_poly2(float x0, float x1, float& y0, float& y1) {
-  constexpr float kRound = 12582912.0f;
-  constexpr int kRoundBits = 0x4B400000;
-  const float c0 = fmaxf(x0, -126.0f), c1 = fmaxf(x1, -126.0f);
-  const uint64_t xc = f2_pack(c0, c1);
-  const uint64_t rb = f2_pack(kRound, kRound), nrb = f2_pack(-kRound, -kRound);
-  const uint64_t t = f2_add(xc, rb);
-  const uint64_t jf = f2_add(t, nrb);
-  float j0, j1, t0, t1;
-  f2_unpack(jf, j0, j1);
-  f2_unpack(t, t0, t1);
-  const uint64_t f = f2_add(xc, f2_pack(-j0, -j1));
-  uint64_t p = f2_fma(f2_pack(0.05517167f, 0.05517167f), f, f2_pack(0.24261114f, 0.24261114f));
-  p = f2_fma(p, f, f2_pack(0.69326099f, 0.69326099f));
-  p = f2_fma(p, f, f2_pack(0.99992807f, 0.99992807f));
-  float p0, p1;
-  f2_unpack(p, p0, p1);
-  const int e0 = __float_as_int(t0) - kRoundBits, e1 = __float_as_int(t1) - kRoundBits;
-  y0 = x0 < -126.0f ? 0.0f : __int_as_float(__float_as_int(p0) + (e0 << 23));
-  y1 = x1 < -126.0f ? 0.0f : __int_as_float(__float_as_int(p1) + (e1 << 23));
 }
 
 }  // namespace lvsa

@@ -10,7 +10,8 @@ It writes ``patterns.npz`` (frame-level ``LVSAMetadata.build`` outputs),
 reference's ``apply_rotary_emb`` / ``slice_rotary_emb`` on seeded inputs)
 and ``adapters.npz`` (the reference HunyuanVideo / CogVideoX adapters on
 seeded mock modules) and ``cp.npz`` (the reference's world > 1 path, per
-rank); ``--only rope|adapters|cp`` writes just one of them.  The fixtures are committed;
+rank) and ``cfg1.npz`` (BASELINE configs[0] at full size, fp32, sampled
+rows); ``--only rope|adapters|cp|cfg1`` writes just one of them.  The fixtures are committed;
 the tests never need the reference at run time.
 """
 
@@ -245,6 +246,51 @@ def adapters_golden(ref_root: str) -> None:
     print("wrote adapters")
 
 
+# B=1, 12 heads, head_dim 128, fp32 q/k/v ~ N(0,1),
+# 9 latent frames x 1560 tokens, W=1, one anchor, kfi 4, step 3.
+CFG1 = dict(T=9, P=1560, H=12, D=128, W=1, n_first=1, kfi=4, step=3, seed=9001, rows_per_frame=24)
+
+
+def cfg1_inputs():
+    """The full-size fp32 inputs, regenerated from the seed (torch's CPU
+    generator is deterministic for a given torch build)."""
+    c = CFG1
+    g = torch.Generator().manual_seed(c["seed"])
+    N = c["T"] * c["P"]
+    return tuple(torch.randn(1, N, c["H"], c["D"], generator=g) for _ in range(3))
+
+
+def cfg1_rows():
+    """Sampled query rows: rows_per_frame seeded token positions in every frame."""
+    c = CFG1
+    rng = np.random.default_rng(c["seed"])
+    return np.concatenate([f * c["P"] + np.sort(rng.choice(c["P"], c["rows_per_frame"], replace=False))
+                           for f in range(c["T"])]).astype(np.int64)
+
+
+def cfg1_golden(ref_root: str) -> None:
+    """configs[0] at full size through the reference's own lvsa_sdpa in fp32
+    (lvsa/sparse_attention.py:643-706), global K/V as _build_global_kv at
+    world 1.  The output is kept on sampled rows (all heads) with checksums
+    of the inputs, so the test can regenerate them and detect a drift."""
+    sys.path.insert(0, ref_root)
+    from lvsa.sparse_attention import LVSAMetadata, lvsa_sdpa
+    c = CFG1
+    q, k, v = cfg1_inputs()
+    m = LVSAMetadata.build(total_latent_frames=c["T"], num_patches=c["P"], window_size=c["W"],
+                           n_first_frames=c["n_first"], key_frame_interval=c["kfi"], rank=0, world=1,
+                           expand_window=True, keyframe_offset=c["step"] % c["kfi"])
+    gi = torch.tensor(m.global_indices, dtype=torch.long)
+    idx = (gi[:, None] * c["P"] + torch.arange(c["P"])[None, :]).flatten()
+    out = lvsa_sdpa(q, k, v, k[:, idx], v[:, idx], m)
+    rows = cfg1_rows()
+    np.savez_compressed(os.path.join(HERE, "cfg1.npz"), rows=rows, out=out[0, rows].numpy(),
+                        checksums=np.asarray([float(x.double().sum()) for x in (q, k, v)]),
+                        params=np.asarray([c[x] for x in ("T", "P", "H", "D", "W", "n_first", "kfi", "step",
+                                                          "seed", "rows_per_frame")]))
+    print("wrote cfg1")
+
+
 class _Pipe:
     """Minimal pipeline stand-in for the geometry helpers."""
 
@@ -265,9 +311,10 @@ if __name__ == "__main__":
     root = args[0] if args else os.environ.get("LVSA_REFERENCE_ROOT", ".")
     if "--only" in sys.argv:
         which = sys.argv[sys.argv.index("--only") + 1]
-        {"rope": rope_golden, "adapters": adapters_golden, "cp": cp_golden}[which](root)
+        {"rope": rope_golden, "adapters": adapters_golden, "cp": cp_golden, "cfg1": cfg1_golden}[which](root)
     else:
         main(root)
         rope_golden(root)
         adapters_golden(root)
         cp_golden(root)
+        cfg1_golden(root)

@@ -142,3 +142,18 @@ def test_flop_counts_baseline_cfg1():
     tiles, exact = O.flop_counts(fp["attended"], 9, 1560, 9 * 1560, 0, 12, 128)
     assert round(exact / 1e9, 1) == 942.0
     assert round(tiles / 1e9, 1) == 964.5
+
+
+def test_oracle_attention_cfg1_full_size_matches_reference():
+    """BASELINE configs[0] at full size (fp32): the oracle on one query frame
+    against the reference's lvsa_sdpa rows kept in tests/golden/cfg1.npz."""
+    from tests.golden.make_golden import CFG1, cfg1_inputs
+    z = np.load(os.path.join(GOLDEN, "cfg1.npz"))
+    q, k, v = (x.numpy() for x in cfg1_inputs())
+    c = CFG1
+    fp = O.frame_pattern(c["T"], c["P"], c["W"], c["n_first"], c["kfi"], c["step"] % c["kfi"])
+    frame = 3
+    want, _ = O.attention(q, k, v, fp, frames=[frame])
+    sel = (z["rows"] // c["P"]) == frame
+    assert sel.sum() == c["rows_per_frame"]
+    np.testing.assert_allclose(want[0, z["rows"][sel]], z["out"][sel], atol=2e-6, rtol=0)
