@@ -216,9 +216,7 @@ def run_b200(args, cfg):
     elif ulysses:
         # Strong scaling: the same 30 layers on every N; each rank holds its
         # contiguous token shard of q/k/v (heads are scattered by all-to-all).
-        from longvideosparseattention_b200.ulysses import shard_sizes, ulysses_attention
-        if H % world:
-            raise SystemExit(f"Ulysses needs heads ({H}) divisible by the GPU count ({world})")
+        from longvideosparseattention_b200.ulysses import mask_local_attention, shard_sizes, ulysses_attention
         sizes = shard_sizes(T * P, world)
         a0 = sum(sizes[:rank])
         layers = []
@@ -235,6 +233,15 @@ def run_b200(args, cfg):
     stream = torch.cuda.current_stream(dev)
     mask = build_block_mask(T, P, cfg["W"], cfg["n_first"], cfg["kfi"], cfg["step"] % cfg["kfi"],
                             True, nt, device=dev)
+    phases = []
+    if ulysses:
+        # Work units (head, tile row) weighted by the row's key-tile count; the
+        # pattern is fixed for the step, so the schedule is made once.
+        from longvideosparseattention_b200.ulysses import make_schedule, tile_costs
+        sched = make_schedule(H, H, world, mask.n_q_tiles, tile_costs(mask))
+        local_attn = mask_local_attention(mask)
+        if rank == 0:
+            log(f"ulysses x{world}: pieces of rank 0 {sched.pieces[0]}")
 
     def step(s, ev=None):
         nonlocal mask
@@ -247,9 +254,10 @@ def run_b200(args, cfg):
             if refcp:
                 cp_attention(lay[0], lay[1], lay[2], shard, gkv, *tx)
             elif ulysses:
-                ulysses_attention(lay[0], lay[1], lay[2], sizes,
-                                  lambda q, k, v, a, b_, c: block_sparse_attention(q, k, v, mask, a, b_, c), *tx,
-                                  chunks=args.chunks)
+                tm = {} if ev is not None else None
+                ulysses_attention(lay[0], lay[1], lay[2], sizes, local_attn, *tx, schedule=sched, timing=tm)
+                if tm is not None:
+                    phases.append(tm)
             else:
                 block_sparse_attention(lay[0], lay[1], lay[2], mask, *tx, out=outs[i & 1], text_out=touts[i & 1],
                                        fp8=args.fp8)
@@ -278,6 +286,17 @@ def run_b200(args, cfg):
     check_device_errors(dev)
     ms = start.elapsed_time(stop)
     kern_ms = [a.elapsed_time(b) for e in evs for (a, b) in e]
+    phase_ms = None
+    if phases:
+        names = ["start", "packed", "exchanged", "attended", "returned", "done"]
+        acc = {n: [] for n in ("pack", "all_to_all_qkv", "attention", "return", "finish")}
+        for tm in phases:
+            for key, (a_, b_) in zip(acc, zip(names[:-1], names[1:])):
+                acc[key].append(tm[a_].elapsed_time(tm[b_]))
+        pm = torch.tensor([statistics.mean(v) for v in acc.values()], device=dev)
+        if world > 1:
+            dist.all_reduce(pm, op=dist.ReduceOp.MAX)
+        phase_ms = {k: round(float(x), 4) for k, x in zip(acc, pm.tolist())}
     t = torch.tensor([ms], device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -295,7 +314,8 @@ def run_b200(args, cfg):
         pk, pk_kind = peaks()
         mean_launch = statistics.mean(kern_ms)
         # per timed layer call: H/world heads under Ulysses (all-to-all included)
-        achieved = flop_tiles / (world if (ulysses or refcp) else 1) / (mean_launch * 1e-3) / 1e12
+        kernel_ms = phase_ms["attention"] if phase_ms else mean_launch
+        achieved = flop_tiles / (world if (ulysses or refcp) else 1) / (kernel_ms * 1e-3) / 1e12
         peak = pk.get("bf16_tflops_sustained", pk.get("bf16_tflops"))
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world,
@@ -304,25 +324,21 @@ def run_b200(args, cfg):
             "scaling": "strong" if (ulysses or refcp) else "weak",
             "vs_baseline": None, "dtype": "e4m3 (QK, PV; fp32 accumulate)" if args.fp8 else "bf16",
             "data": "synthetic (seeded N(0,1)/sqrt(D), RoPE-3D)",
-            "config": {"workload": args.config, "desc": cfg["desc"], "layers_per_step": L,
-                       "tokens": T * P + nt, "heads": H, "head_dim": D, "tile": "128x128",
-                       "flop_tiles_per_layer": flop_tiles, "flop_exact_per_layer": flop_exact,
-                       "l2": "30 distinct layer inputs (35 GB) cycled: inputs exceed L2, no flush",
-                       "parallelism": (f"ulysses x{world} (heads scattered by NCCL all-to-all, "
-                                        f"chunks={args.chunks or 'auto'})" if ulysses
-                                       else (f"reference CP x{world} (token shards, global frames by NCCL "
-                                             "all-reduce, rank-local windows; FLOPs of that pattern)") if refcp
-                                       else f"replicas x{world} (independent layers per rank)")},
+            "config": bench_config(args, cfg, world, flop_tiles, flop_exact),
             "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak,
                          "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
                          "traffic": NCU_TRAFFIC_BYTES.get(args.config),
                          "algorithmic_bytes": 4 * T * P * H * D * 2 + 4 * nt * H * D * 2,
                          "peak_source": f"{pk_kind} bf16_tflops_sustained (kernel runs back-to-back in a long step)",
-                         "mean_launch_ms": round(mean_launch, 4)},
+                         "mean_launch_ms": round(kernel_ms, 4)},
             "clocks": clk.summary(),
-            "gpu_launches": (4 + L * (7 if args.fp8 else (2 if refcp and nt else 1))) * args.steps,
+            "gpu_launches": (4 + L * (7 if args.fp8 else (2 if refcp and nt else
+                                                        (len(sched.pieces[0]) + 3 if ulysses else 1)))) * args.steps,
             "e2e": e2e,
         }
+        if phase_ms:
+            line["ulysses_phases_ms_per_layer"] = phase_ms
+            line["nccl"] = {"backend": "nccl", "world": world, "version": ".".join(map(str, torch.cuda.nccl.version()))}
         if args.cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(cfg, flop_tiles, budget_s=args.cpu_seconds)
         print(json.dumps(line), flush=True)
@@ -381,9 +397,7 @@ def run_e2e(args, cfg, dev, world, flop_tiles):
 _CPU_INPUTS = {}
 
 
-def cpu_sample(cfg, frames, threads):
-    """Time the reference's CPU arithmetic (oracle restatement of lvsa_sdpa:
-    per-frame K/V concat + torch fp32 SDPA) for `frames` query frames."""
+def _cpu_setup(cfg, threads):
     import torch
     from oracle import lvsa_oracle as O
     T, P, H, D, nt = cfg["T"], cfg["P"], cfg["H"], cfg["D"], cfg["n_text"]
@@ -394,54 +408,115 @@ def cpu_sample(cfg, frames, threads):
         sc = 1.0 / math.sqrt(D)
         mk = lambda n: torch.randn(1, n, H, D, generator=g) * sc
         _CPU_INPUTS[key] = (mk(T * P), mk(T * P), mk(T * P), mk(nt) if nt else None, mk(nt) if nt else None)
-    q, k, v, tk, tv = _CPU_INPUTS[key]
     fp = O.frame_pattern(T, P, cfg["W"], cfg["n_first"], cfg["kfi"], cfg["step"] % cfg["kfi"])
+    return _CPU_INPUTS[key], fp
+
+
+def frame_flops(cfg, fp, f):
+    """Useful FLOPs of query frame f on the CPU path: 4 D H P x (its keys)."""
+    P, H, D, nt = cfg["P"], cfg["H"], cfg["D"], cfg["n_text"]
+    lo, hi = (int(x) for x in fp["window_bounds"][f])
+    win = [w for w in range(lo, hi + 1) if w not in fp["global_set"]]
+    keys = (len(fp["global_indices"]) + len(win)) * P + nt
+    return 4 * D * H * P * keys
+
+
+def cpu_sample(cfg, frames, threads):
+    """Time the reference's CPU arithmetic (oracle restatement of lvsa_sdpa:
+    per-frame K/V concat + torch fp32 SDPA) for `frames` query frames;
+    returns (seconds, useful FLOPs of those frames)."""
+    from oracle import lvsa_oracle as O
+    (q, k, v, tk, tv), fp = _cpu_setup(cfg, threads)
     t0 = time.perf_counter()
     O.attention_torch_cpu(q, k, v, fp, tk, tv, frames=frames)
-    return time.perf_counter() - t0
+    return time.perf_counter() - t0, sum(frame_flops(cfg, fp, f) for f in frames)
+
+
+def _spread(T, n, phase=0):
+    """n query frames spread over [0, T), shifted by `phase`."""
+    n = max(1, min(T, n))
+    return sorted({(int(round(i * T / n)) + phase) % T for i in range(n)})
 
 
 def cpu_baseline(cfg, flop_tiles, budget_s=15.0):
     threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
     T = cfg["T"]
-    t1 = cpu_sample(cfg, [T // 2], threads)
-    nf = max(1, min(T, int(budget_s / max(t1, 1e-3))))
-    frames = [int(round(i * (T - 1) / max(1, nf - 1))) for i in range(nf)] if nf > 1 else [T // 2]
-    t = cpu_sample(cfg, frames, threads)
-    # per-frame work is identical (constant attended count), so scale by T / frames
-    per_layer = t * T / len(frames)
-    return {"value": round(flop_tiles / per_layer / 1e12, 4), "unit": "TFLOP/s", "cores": threads,
-            "kind": "port", "ms_per_layer": round(per_layer * 1e3, 1),
-            "sample": f"{len(frames)} of {T} query frames x all heads of one {cfg['desc']} layer: "
-                      f"lvsa_sdpa restated (K/V concat + torch fp32 CPU SDPA), scaled by T/frames"}
+    t1, _ = cpu_sample(cfg, [T // 2], threads)
+    frames = _spread(T, int(budget_s / max(t1, 1e-3)))
+    t, fl = cpu_sample(cfg, frames, threads)
+    # The CPU computes exactly the attended keys: time a layer at that rate
+    # (its exact FLOPs), then report the layer's FLOP_tiles over that time,
+    # the unit of the GPU arm's value.
+    _, flop_exact = flops_for(cfg)
+    layer_s = flop_exact / (fl / t)
+    return {"value": round(flop_tiles / layer_s / 1e12, 4), "unit": "TFLOP/s", "cores": threads,
+            "kind": "port", "ms_per_layer_extrapolated": round(layer_s * 1e3, 1),
+            "sample": f"{len(frames)} of {T} query frames x all heads of one {cfg['desc']} layer "
+                      f"({t:.1f} s): lvsa_sdpa restated (K/V concat + torch fp32 CPU SDPA); "
+                      "value = the layer's FLOP_tiles / (its exact FLOPs at the measured rate)"}
 
 
 def run_reference(args, cfg):
+    """The reference's CPU implementation of the path (lvsa_sdpa's per-frame
+    K/V concat + torch fp32 SDPA, restated by the oracle port) on all host
+    cores.  Each step times K_FRAMES query frames (all heads) of one layer,
+    a different spread of frames per step.  ``ms_per_step`` is the time
+    actually measured per step; ``ms_per_layer`` extrapolates it to the
+    layer (its exact FLOPs at the measured rate) and ``value`` is the
+    layer's FLOP_tiles over that time, the GPU arm's unit."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
+    K_FRAMES = 3
     flop_tiles, flop_exact = flops_for(cfg)
     threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
     T = cfg["T"]
-    per = []
+    secs, flops = [], []
     for s in range(args.warmup + args.steps):
-        f = [(s * 7) % T]
-        dt = cpu_sample(cfg, f, threads)
+        dt, fl = cpu_sample(cfg, _spread(T, K_FRAMES, phase=5 * s), threads)
         if s >= args.warmup:
-            per.append(dt * T)  # seconds per layer
-    per_layer = statistics.mean(per)
-    val = flop_tiles / per_layer / 1e12
+            secs.append(dt)
+            flops.append(fl)
+    layer_s = flop_exact / (sum(flops) / sum(secs))   # exact keys at the measured rate
+    val = flop_tiles / layer_s / 1e12                   # in the GPU arm's unit (FLOP_tiles / time)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     line = {"impl": "reference", "metric": METRIC, "value": round(val, 4), "unit": "TFLOP/s",
-            "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(per_layer * 1e3 * cfg["layers"], 1),
-            "ms_per_layer": round(per_layer * 1e3, 1), "higher_is_better": True, "scaling": "weak",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(statistics.mean(secs) * 1e3, 1),
+            "ms_per_layer": round(layer_s * 1e3, 1), "extrapolated": True,
+            "extrapolation": f"ms_per_layer = the layer's exact FLOPs / the measured rate; each timed step is "
+                             f"{K_FRAMES} of {T} query frames",
+            "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1)/sqrt(D))",
-            "config": {"workload": args.config, "desc": cfg["desc"], "layers_per_step": cfg["layers"]},
+            "config": bench_config(args, cfg, world, flop_tiles, flop_exact),
             "cpu_baseline": {"value": round(val, 4), "unit": "TFLOP/s", "cores": threads, "kind": "port",
-                             "sample": "1 query frame (all heads) per step of one layer, scaled by T"},
+                             "sample": f"{K_FRAMES} query frames (all heads) of one layer per step"},
             "e2e": {"value": round(val, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+def bench_config(args, cfg, world, flop_tiles, flop_exact, parallelism=None):
+    """The `config` object both arms print (same keys and values for one N)."""
+    T, P, H, D, nt = cfg["T"], cfg["P"], cfg["H"], cfg["D"], cfg["n_text"]
+    if parallelism is None:
+        parallelism = _parallelism(args, world, H)
+    return {"workload": args.config, "desc": cfg["desc"], "layers_per_step": cfg["layers"],
+            "tokens": T * P + nt, "heads": H, "head_dim": D, "tile": "128x128",
+            "flop_tiles_per_layer": flop_tiles, "flop_exact_per_layer": flop_exact,
+            "l2": "30 distinct layer inputs (35 GB) cycled: inputs exceed L2, no flush",
+            "parallelism": parallelism}
+
+
+def _parallelism(args, world, H):
+    if world > 1 and args.parallel == "ulysses":
+        return (f"ulysses x{world} (NCCL all-to-all of q/k/v and of the output; "
+                + ("whole heads per rank)" if H % world == 0
+                   else "(head, tile-row) units balanced by key-tile count)"))
+    if world > 1 and args.parallel == "cp":
+        return (f"reference CP x{world} (token shards, global frames by NCCL all-reduce, "
+                "rank-local windows; FLOPs of that pattern)")
+    return f"replicas x{world} (independent layers per rank)"
 
 
 def run_prologue(args, cfg):
@@ -529,14 +604,12 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--fp8", action="store_true",
                     help="E4M3 QK/PV with per-tile scales (quantisation inside the timed step)")
-    ap.add_argument("--parallel", default="replicas", choices=["replicas", "ulysses", "cp"],
-                    help="N>1: independent layers per rank (weak scaling), Ulysses head "
-                         "parallelism over one set of layers (strong scaling), or the reference's "
-                         "own sequence-shard pattern (cp, strong scaling)")
+    ap.add_argument("--parallel", default="ulysses", choices=["replicas", "ulysses", "cp"],
+                    help="N>1: Ulysses head parallelism over one set of layers (default, strong "
+                         "scaling), the reference's own sequence-shard pattern (cp, strong scaling), "
+                         "or independent layers per rank (replicas, weak scaling)")
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
-    ap.add_argument("--chunks", type=int, default=None,
-                    help="Ulysses: head groups exchanged while the previous group computes (default: auto)")
     ap.add_argument("--prologue", action="store_true",
                     help="time the fused QK prologue (norm + RoPE) instead of the attention step")
     args = ap.parse_args()

@@ -127,6 +127,11 @@ typedef struct LvsaAttnArgs {
   int32_t token_offset;
   /* First tile-CSR row to compute (rows [first_q_tile, n_q_tiles)); 0: all. */
   int32_t first_q_tile;
+  /* One past the last tile-CSR row to compute (ABI 102); <= 0: n_q_tiles.
+   * With first_q_tile it selects a row range, e.g. one rank's share of a
+   * head under head-and-tile partitioned Ulysses parallelism.  Rows outside
+   * the range (and their LSE entries) are not written. */
+  int32_t end_q_tile;
 } LvsaAttnArgs;
 
 /* Block-sparse attention forward on tcgen05/TMEM, K/V read in place.
@@ -239,6 +244,23 @@ int lvsa_qk_prologue(const LvsaQkPrologue* args, void* stream);
  *  - head_dim 128 only, as lvsa_attn_fwd_fp8. */
 #define LVSA_NOALLOC_SCRATCH_BYTES (96u * 1024u * 1024u)
 int lvsa_attn_fwd_fp8_noalloc(const LvsaAttnArgs* args, void* stream);
+
+/* ---- batched strided row copies (gather / scatter of an exchange) ----
+ * No counterpart in the reference (its only multi-GPU exchange is one
+ * all_reduce).  Packs and unpacks the Ulysses all-to-all buffers in one
+ * launch: each segment copies batch x rows x heads vectors of `row_bytes`
+ * from src to dst, element (b, t, h) at byte offset b*sb + t*st + h*sh of
+ * each side.  Pointers, strides and row_bytes must be multiples of 16 bytes;
+ * segments must not overlap in dst. */
+#define LVSA_MAX_COPY_SEGMENTS 64
+typedef struct LvsaCopySegment {
+  const void* src;
+  void* dst;
+  int64_t src_sb, src_st, src_sh;  /* byte strides */
+  int64_t dst_sb, dst_st, dst_sh;
+  int32_t batch, rows, heads;
+} LvsaCopySegment;
+int lvsa_copy_segments(const LvsaCopySegment* segs, int32_t n, int32_t row_bytes, void* stream);
 
 /* Human-readable name of a status code. */
 const char* lvsa_status_str(int status);

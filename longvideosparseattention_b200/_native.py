@@ -27,7 +27,7 @@ LVSA_DTYPE_F16 = 1
 LVSA_MAX_FRAMES = 2048
 
 EXPORTED_SYMBOLS = ("lvsa_mask_layout", "lvsa_build_mask", "lvsa_attn_fwd", "lvsa_quantize_e4m3",
-                    "lvsa_attn_fwd_fp8", "lvsa_attn_fwd_fp8_noalloc", "lvsa_qk_prologue", "lvsa_status_str",
+                    "lvsa_attn_fwd_fp8", "lvsa_attn_fwd_fp8_noalloc", "lvsa_qk_prologue", "lvsa_copy_segments", "lvsa_status_str",
                     "lvsa_abi_version")
 LVSA_DTYPE_E4M3 = 2
 LVSA_DTYPE_F32 = 3
@@ -69,7 +69,17 @@ class LvsaAttnArgs(ctypes.Structure):
                 ("block_q", _i32), ("block_k", _i32), ("n_q_video_tiles", _i32),
                 ("n_q_tiles", _i32), ("n_k_video_tiles", _i32),
                 ("frame_bits", _vp), ("tile_indptr", _vp), ("tile_indices", _vp),
-                ("tile_flags", _vp), ("error_word", _vp), ("token_offset", _i32), ("first_q_tile", _i32)]
+                ("tile_flags", _vp), ("error_word", _vp), ("token_offset", _i32), ("first_q_tile", _i32),
+                ("end_q_tile", _i32)]
+
+
+LVSA_MAX_COPY_SEGMENTS = 64
+
+
+class LvsaCopySegment(ctypes.Structure):
+    _fields_ = [("src", _vp), ("dst", _vp), ("src_sb", _i64), ("src_st", _i64), ("src_sh", _i64),
+                ("dst_sb", _i64), ("dst_st", _i64), ("dst_sh", _i64), ("batch", _i32), ("rows", _i32),
+                ("heads", _i32)]
 
 
 class LvsaQkPrologue(ctypes.Structure):
@@ -120,6 +130,8 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
         lib.lvsa_attn_fwd_fp8_noalloc.restype = ctypes.c_int
         lib.lvsa_qk_prologue.argtypes = [ctypes.POINTER(LvsaQkPrologue), _vp]
         lib.lvsa_qk_prologue.restype = ctypes.c_int
+        lib.lvsa_copy_segments.argtypes = [ctypes.POINTER(LvsaCopySegment), _i32, _i32, _vp]
+        lib.lvsa_copy_segments.restype = ctypes.c_int
         lib.lvsa_status_str.argtypes = [ctypes.c_int]
         lib.lvsa_status_str.restype = ctypes.c_char_p
         lib.lvsa_abi_version.argtypes = []

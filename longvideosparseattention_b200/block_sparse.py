@@ -219,7 +219,8 @@ def block_sparse_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, ma
                            text_v: Optional[torch.Tensor] = None,
                            scale: Optional[float] = None, return_lse: bool = False,
                            out: Optional[torch.Tensor] = None,
-                           text_out: Optional[torch.Tensor] = None, fp8: bool = False):
+                           text_out: Optional[torch.Tensor] = None, fp8: bool = False,
+                           q_tiles: Optional[Tuple[int, int]] = None):
     """LVSA attention of one layer on the GPU.
 
     q [B, Nv, H, D], k/v [B, Nv, Hkv, D] (video, frame-major tokens);
@@ -228,6 +229,10 @@ def block_sparse_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, ma
     are rounded to bf16 and the output is returned in the input dtype.
     Returns (out, text_out) or, with ``return_lse``, (out, text_out, lse,
     text_lse) where lse is natural-log [B, H, N] fp32.
+
+    ``q_tiles=(t0, t1)`` computes only tile-CSR rows [t0, t1) (video rows
+    first, then text rows); the other rows of ``out`` / ``text_out`` are
+    left as they are, so pass them to keep their contents.
     """
     if not q.is_cuda:
         raise RuntimeError("block_sparse_attention needs CUDA tensors (no CPU fallback)")
@@ -279,7 +284,9 @@ def block_sparse_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, ma
         mask.n_q_video_tiles, mask.n_q_tiles, mask.n_k_video_tiles,
         mask.frame_bits.data_ptr(), mask.tile_indptr.data_ptr(), mask.tile_indices.data_ptr(),
         mask.tile_flags.data_ptr(), error_word(q.device).data_ptr(),
-        getattr(mask, "token_offset", 0), getattr(mask, "first_q_tile", 0))
+        getattr(mask, "token_offset", 0),
+        int(q_tiles[0]) if q_tiles is not None else getattr(mask, "first_q_tile", 0),
+        int(q_tiles[1]) if q_tiles is not None else 0)
     with torch.cuda.device(q.device):
         if fp8:
             st = N.load().lvsa_attn_fwd_fp8(ctypes.byref(args), ctypes.byref(sc_c), _stream_ptr(q.device))
@@ -302,3 +309,35 @@ def block_sparse_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, ma
 
 def default_scale(head_dim: int) -> float:
     return 1.0 / math.sqrt(head_dim)
+
+
+def copy_segments(segments: Sequence[Tuple[torch.Tensor, torch.Tensor]]) -> None:
+    """dst.copy_(src) for every (src, dst) pair of [B, N, H, D] views, in one
+    launch of the batched strided copy kernel (CUDA tensors; strides and
+    pointers multiples of 16 bytes).  CPU tensors (the gloo test ranks) are
+    copied by torch."""
+    segs = [(s, d) for s, d in segments if s.numel()]
+    if not segs:
+        return
+    if not segs[0][0].is_cuda:
+        for s, d in segs:
+            d.copy_(s)
+        return
+    dev = segs[0][0].device
+    es = segs[0][0].element_size()
+    D = segs[0][0].shape[-1]
+    lib = N.load()
+    for i in range(0, len(segs), N.LVSA_MAX_COPY_SEGMENTS):
+        chunk = segs[i:i + N.LVSA_MAX_COPY_SEGMENTS]
+        arr = (N.LvsaCopySegment * len(chunk))()
+        for j, (s, d) in enumerate(chunk):
+            if s.shape != d.shape or s.dim() != 4 or s.stride(-1) != 1 or d.stride(-1) != 1 \
+                    or s.shape[-1] != D or s.dtype != d.dtype:
+                raise ValueError("copy_segments: matching [B, N, H, D] views with a contiguous last dim")
+            arr[j] = N.LvsaCopySegment(s.data_ptr(), d.data_ptr(),
+                                       s.stride(0) * es, s.stride(1) * es, s.stride(2) * es,
+                                       d.stride(0) * es, d.stride(1) * es, d.stride(2) * es,
+                                       s.shape[0], s.shape[1], s.shape[2])
+        with torch.cuda.device(dev):
+            st = lib.lvsa_copy_segments(arr, len(chunk), D * es, _stream_ptr(dev))
+        N.check(st, "lvsa_copy_segments")

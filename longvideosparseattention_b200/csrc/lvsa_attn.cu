@@ -1058,7 +1058,8 @@ int launch(const LvsaAttnArgs* a, cudaStream_t stream, const LvsaFp8Scales* sc =
 
   p.tok_off = a->token_offset;
   p.row0 = a->first_q_tile;
-  const int end = text_rows ? a->n_q_tiles : a->n_q_video_tiles;
+  const int end = std::min(text_rows ? a->n_q_tiles : a->n_q_video_tiles,
+                           a->end_q_tile > 0 ? a->end_q_tile : a->n_q_tiles);
   const int rows = end - a->first_q_tile;
   if (rows <= 0) return LVSA_OK;
   p.pair_end = end;
@@ -1104,6 +1105,8 @@ int validate(const LvsaAttnArgs* a) {
       a->token_offset + static_cast<long long>(a->n_video) > grid_tokens)
     return LVSA_ERR_GEOMETRY;
   if (a->first_q_tile < 0 || a->first_q_tile > a->n_q_tiles) return LVSA_ERR_INVALID_ARG;
+  if (a->end_q_tile > 0 && (a->end_q_tile < a->first_q_tile || a->end_q_tile > a->n_q_tiles))
+    return LVSA_ERR_INVALID_ARG;
   if (a->n_q_video_tiles != (a->n_video + kBlockQ - 1) / kBlockQ || a->n_k_video_tiles != (a->n_video + kBN - 1) / kBN ||
       a->frame_words != (a->total_frames + 31) / 32)
     return LVSA_ERR_GEOMETRY;
@@ -1212,4 +1215,4 @@ extern "C" const char* lvsa_status_str(int status) {
   }
 }
 
-extern "C" int lvsa_abi_version(void) { return 101; }
+extern "C" int lvsa_abi_version(void) { return 102; }

@@ -171,13 +171,23 @@ class DistributedLVSAProcessor:
             nt = 0 if enc_k is None else int(enc_k.shape[1])
             return block_sparse_attention(query, key, value, self.block_mask(query.device, nt),
                                           enc_q, enc_k, enc_v)
-        from .ulysses import shard_sizes, ulysses_attention
+        from .ulysses import shard_sizes, tile_costs, ulysses_attention
+        nt = 0 if enc_k is None else int(enc_k.shape[1])
+        mask = self.block_mask(query.device, nt)
 
-        def local(q, k, v, tq, tk, tv):
-            nt = 0 if tk is None else int(tk.shape[1])
-            return block_sparse_attention(q, k, v, self.block_mask(q.device, nt), tq, tk, tv)
+        def local(q, k, v, tq, tk, tv, q_tiles, out, text_out):
+            block_sparse_attention(q, k, v, mask, tq, tk, tv, out=out, text_out=text_out, q_tiles=q_tiles)
+        costs = None
+        if query.shape[2] % self.world:
+            # Head count not divisible by the GPU count: balance (head, tile row)
+            # units by each row's key-tile count, read once per pattern.
+            ck = (self._metadata.keyframe_offset, nt, query.device)
+            if getattr(self, "_costs_key", None) != ck:
+                self._costs, self._costs_key = tile_costs(mask), ck
+            costs = self._costs
         sizes = shard_sizes(self.total_num_frames * self.num_patches, self.world)
-        return ulysses_attention(query, key, value, sizes, local, enc_q, enc_k, enc_v)
+        return ulysses_attention(query, key, value, sizes, local, enc_q, enc_k, enc_v,
+                                 n_q_tiles=mask.n_q_tiles, costs=costs)
 
     @staticmethod
     def _dense(query, key, value):

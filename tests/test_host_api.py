@@ -122,7 +122,7 @@ def test_library_exports_every_header_symbol():
     nm = subprocess.run(["nm", "-D", "--defined-only", _native.LIB_PATH], capture_output=True, text=True)
     exported = set(re.findall(r" T (lvsa_\w+)", nm.stdout))
     assert declared <= exported
-    assert lib.lvsa_abi_version() == 101
+    assert lib.lvsa_abi_version() == 102
     assert lib.lvsa_status_str(0) == b"ok"
 
 
@@ -136,8 +136,8 @@ def test_struct_layouts_match_header():
 int main(void){
  printf("%zu %zu %zu %zu %zu\n", sizeof(LvsaPattern), sizeof(LvsaMaskLayout), sizeof(LvsaMaskBuffers),
         sizeof(LvsaTensor), sizeof(LvsaAttnArgs));
- printf("%zu %zu %zu\n", offsetof(LvsaAttnArgs, scale), offsetof(LvsaAttnArgs, frame_bits),
-        offsetof(LvsaAttnArgs, error_word));
+ printf("%zu %zu %zu %zu %zu\n", offsetof(LvsaAttnArgs, scale), offsetof(LvsaAttnArgs, frame_bits),
+        offsetof(LvsaAttnArgs, error_word), offsetof(LvsaAttnArgs, end_q_tile), sizeof(LvsaCopySegment));
  return 0;}
 '''
     import tempfile
@@ -151,7 +151,8 @@ int main(void){
     got = [int(x) for x in out]
     want = [ctypes.sizeof(N.LvsaPattern), ctypes.sizeof(N.LvsaMaskLayout),
             ctypes.sizeof(N.LvsaMaskBuffers), ctypes.sizeof(N.LvsaTensor), ctypes.sizeof(N.LvsaAttnArgs),
-            N.LvsaAttnArgs.scale.offset, N.LvsaAttnArgs.frame_bits.offset, N.LvsaAttnArgs.error_word.offset]
+            N.LvsaAttnArgs.scale.offset, N.LvsaAttnArgs.frame_bits.offset, N.LvsaAttnArgs.error_word.offset,
+            N.LvsaAttnArgs.end_q_tile.offset, ctypes.sizeof(N.LvsaCopySegment)]
     assert got == want
 
 
@@ -172,7 +173,7 @@ def test_mask_layout_host_call_and_errors():
 
 
 def test_noalloc_entry_rejects_oversize_before_any_cuda_call():
-    """The fixed-scratch FP8 entry checks its limit before touching CUDA, so
+    """The fixed-scratch FP8 entry checks its arguments, geometry and limit before touching CUDA, so
     this runs without a GPU; the pointers are never dereferenced."""
     import ctypes
     from longvideosparseattention_b200 import _native as N
@@ -181,8 +182,14 @@ def test_noalloc_entry_rejects_oversize_before_any_cuda_call():
     a = N.LvsaAttnArgs()
     a.q = a.k = a.v = a.o = fake
     a.batch, a.n_video, a.n_text, a.heads, a.kv_heads, a.head_dim, a.dtype = 1, 126360, 0, 12, 12, 128, 0
+    a.total_frames, a.num_patches, a.frame_words, a.block_q, a.block_k = 81, 1560, 3, 128, 128
+    a.n_q_video_tiles = a.n_q_tiles = a.n_k_video_tiles = 988
+    a.frame_bits = a.tile_indptr = a.tile_indices = a.tile_flags = 16
     # E4M3 q, k and v alone: 3 x 126360 x 12 x 128 bytes = 582 MB > 96 MiB
     assert lib.lvsa_attn_fwd_fp8_noalloc(ctypes.byref(a), None) == N.LVSA_ERR_CAPACITY
     a.head_dim = 64
     assert lib.lvsa_attn_fwd_fp8_noalloc(ctypes.byref(a), None) == N.LVSA_ERR_UNSUPPORTED
     assert lib.lvsa_attn_fwd_fp8_noalloc(None, None) == N.LVSA_ERR_INVALID_ARG
+    a.head_dim = 128
+    a.n_q_video_tiles = 987           # geometry checked before capacity and before any launch
+    assert lib.lvsa_attn_fwd_fp8_noalloc(ctypes.byref(a), None) == N.LVSA_ERR_GEOMETRY
