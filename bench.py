@@ -309,6 +309,8 @@ def run_b200(args, cfg):
     e2e = None
     if not args.no_e2e and not (ulysses or refcp):
         e2e = run_e2e(args, cfg, dev, world, flop_tiles)
+    elif not args.no_e2e and ulysses:
+        e2e = run_e2e_ulysses(args, cfg, dev, world, rank, flop_tiles, sizes, sched, local_attn)
 
     if rank == 0:
         pk, pk_kind = peaks()
@@ -392,6 +394,55 @@ def run_e2e(args, cfg, dev, world, flop_tiles):
     val = flop_tiles * L * steps * world / (ms * 1e-3) / 1e12
     return {"value": round(val, 2), "unit": "TFLOP/s", "ms_per_layer": round(ms / steps / L, 3),
             "h2d_bytes_per_step": h2d * L, "d2h_bytes_per_step": d2h * L, "steps": steps}
+
+
+def run_e2e_ulysses(args, cfg, dev, world, rank, flop_tiles, sizes, sched, local_attn):
+    """Ulysses through the public call with this rank's token shard in pinned
+    host memory: per layer, H2D of the q/k/v (+text) shard, the head-parallel
+    layer (both all-to-alls inside), D2H of the output shard; all in the
+    timed region, max over ranks."""
+    import torch
+    import torch.distributed as dist
+    from longvideosparseattention_b200.ulysses import ulysses_attention
+    L, nt = cfg["layers"], cfg["n_text"]
+    a0 = sum(sizes[:rank])
+    host = []
+    for i in range(2):
+        lay = seeded_layer(cfg, 10_000 + i, dev)
+        lay[:3] = [x[:, a0:a0 + sizes[rank]] for x in lay[:3]]
+        host.append([x.cpu().pin_memory() for x in lay])
+        del lay
+    out_h = torch.empty(host[0][0].shape, dtype=torch.bfloat16).pin_memory()
+    h2d = sum(x.numel() * x.element_size() for x in host[0])
+    d2h = out_h.numel() * 2 + (host[0][3].numel() * 2 if nt else 0)
+    tout_h = torch.empty(host[0][3].shape, dtype=torch.bfloat16).pin_memory() if nt else None
+
+    def step():
+        for i in range(L):
+            d = [x.to(dev, non_blocking=True) for x in host[i & 1]]
+            tx = (d[3], d[4], d[5]) if nt else (None, None, None)
+            o, to = ulysses_attention(d[0], d[1], d[2], sizes, local_attn, *tx, schedule=sched)
+            out_h.copy_(o, non_blocking=True)
+            if nt:
+                tout_h.copy_(to, non_blocking=True)
+
+    steps = max(1, min(args.steps, 2))
+    step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        step()
+    b.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([a.elapsed_time(b)], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    return {"value": round(flop_tiles * L * steps / (ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+            "ms_per_layer": round(ms / steps / L, 3), "h2d_bytes_per_step": h2d * L * world,
+            "d2h_bytes_per_step": d2h * L * world, "steps": steps,
+            "path": "ulysses_attention on per-rank pinned host shards (copies serialised with the layer)"}
 
 
 _CPU_INPUTS = {}

@@ -90,16 +90,22 @@ def _dense_cols(n_dense: int, nkv: int, BK: int) -> List[Tuple[int, int]]:
 
 def build_shard_pattern(T: int, P: int, W: int, n_first: int, kfi: Optional[int], offset: int,
                         rank: int, world: int, n_text: int = 0, expand: bool = True,
-                        device: Optional[torch.device] = None) -> ShardPattern:
+                        device: Optional[torch.device] = None,
+                        global_indices: Optional[List[int]] = None) -> ShardPattern:
     """Host build (per rank and denoising step, like the reference's
-    LVSAMetadata.build) of the two launches' tile CSRs."""
+    LVSAMetadata.build) of the two launches' tile CSRs.  ``global_indices``
+    (keyframes and boundary guards, e.g. a reference LVSAMetadata's) replaces
+    the global frames derived from n_first / kfi / offset."""
     total = T * P
     if total % world:
         raise AssertionError(f"total_seq={total} (T={T} x P={P}) must be divisible by world={world}.")
     S_r = total // world
     gts = rank * S_r
     guards = compute_boundary_guard_frames(T, S_r, P, world, W)
-    globals_ = sorted(set(compute_global_indices(T, n_first, kfi, offset)) | set(guards))
+    if global_indices is not None:
+        globals_ = sorted(set(int(g) for g in global_indices))
+    else:
+        globals_ = sorted(set(compute_global_indices(T, n_first, kfi, offset)) | set(guards))
     gset = set(globals_)
     # Frames a query frame attends inside the shard: its window minus globals.
     allowed = []

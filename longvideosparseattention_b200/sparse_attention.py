@@ -15,6 +15,7 @@ Same names, signatures and error behaviour as the reference:
 from __future__ import annotations
 
 import math
+from collections import OrderedDict
 from dataclasses import dataclass, field
 from typing import Any, Dict, List, Optional, Sequence, Set, Tuple
 
@@ -333,6 +334,69 @@ def tile_flop_counts(meta: LVSAMetadata, n_text: int, heads: int, head_dim: int,
 # --------------------------------------------------------------------------
 
 
+# Masks of metadata objects that carry no GPU mask of their own (the
+# reference's LVSAMetadata), keyed by the pattern they describe.
+_FOREIGN_MASKS: "OrderedDict[tuple, Any]" = OrderedDict()
+_FOREIGN_CAP = 32
+
+
+def pattern_key(metadata: Any) -> tuple:
+    """The pattern an LVSAMetadata (this package's or the reference's,
+    lvsa/sparse_attention.py:286-353) describes, from fields both carry:
+    geometry, shard, and the global frame list.  The reference object stores
+    neither the keyframe interval nor the offset, but its global_indices
+    (keyframes, anchors and boundary guards) and W / expand_window determine
+    every window bound (lvsa/sparse_attention.py:52-104), hence the whole
+    pattern."""
+    return (int(metadata.total_latent_frames), int(metadata.num_patches), int(metadata.window_size),
+            bool(metadata.expand_window), tuple(int(g) for g in metadata.global_indices),
+            int(metadata.rank), int(metadata.world))
+
+
+def _cached(key: tuple, make):
+    m = _FOREIGN_MASKS.get(key)
+    if m is None:
+        m = make()
+        _FOREIGN_MASKS[key] = m
+        while len(_FOREIGN_MASKS) > _FOREIGN_CAP:
+            _FOREIGN_MASKS.popitem(last=False)
+    else:
+        _FOREIGN_MASKS.move_to_end(key)
+    return m
+
+
+def mask_for(metadata: Any, device: torch.device, n_text: int = 0) -> BlockMask:
+    """World = 1 GPU mask for any LVSAMetadata: this package's (its own
+    cache) or a foreign one such as the reference's, rebuilt on the GPU from
+    ``pattern_key`` with the global frames passed as explicit globals (no
+    anchors, no keyframe grid) and cached by pattern."""
+    if isinstance(metadata, LVSAMetadata):
+        return metadata.block_mask(device, n_text)
+    T, P, W, expand, gidx, _, world = pattern_key(metadata)
+    if world != 1:
+        raise ValueError("mask_for: world = 1 metadata expected (shards go through shard_pattern_for)")
+    device = torch.device(device)
+    if device.index is None:
+        device = torch.device("cuda", torch.cuda.current_device())
+    return _cached(pattern_key(metadata) + ("mask", str(device), int(n_text)),
+                   lambda: build_block_mask(T, P, W, 0, None, 0, expand, n_text,
+                                            boundary_guards=list(gidx), device=device))
+
+
+def shard_pattern_for(metadata: Any, device: torch.device, n_text: int = 0):
+    """Sequence-shard (world > 1) launch pattern of a rank's metadata: the
+    reference's own context-parallel semantics (``cp_mode``), with the
+    metadata's global frames (keyframes + boundary guards) taken as given."""
+    from .cp_mode import build_shard_pattern
+    T, P, W, expand, gidx, rank, world = pattern_key(metadata)
+    device = torch.device(device)
+    if device.index is None:
+        device = torch.device("cuda", torch.cuda.current_device())
+    return _cached(pattern_key(metadata) + ("shard", str(device), int(n_text)),
+                   lambda: build_shard_pattern(T, P, W, 0, None, 0, rank, world, n_text, expand,
+                                               device=device, global_indices=list(gidx)))
+
+
 def _text_part(k_global: Optional[torch.Tensor], metadata: LVSAMetadata) -> int:
     if k_global is None:
         return 0
@@ -350,13 +414,15 @@ def lvsa_attention(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor,
                    text_key: Optional[torch.Tensor] = None, text_value: Optional[torch.Tensor] = None,
                    scale: Optional[float] = None, return_lse: bool = False):
     """Video rows (sparse, plus all text) and optional text rows (dense) of one
-    layer in a single kernel launch.  Full-sequence (world = 1) tensors."""
+    layer in a single kernel launch.  Full-sequence (world = 1) tensors;
+    ``metadata`` is this package's LVSAMetadata or the reference's."""
     if metadata.world != 1:
         raise NotImplementedError(
-            "the block-sparse kernel takes the full sequence; for context parallelism use "
-            "longvideosparseattention_b200.ulysses (head-parallel all-to-all)")
+            "lvsa_attention takes the full sequence; for context parallelism use "
+            "longvideosparseattention_b200.ulysses (head-parallel all-to-all) or lvsa_sdpa with "
+            "the rank's metadata and its gathered global K/V")
     nt = 0 if text_key is None else int(text_key.shape[1])
-    mask = metadata.block_mask(query.device, nt)
+    mask = mask_for(metadata, query.device, nt)
     return block_sparse_attention(query, key, value, mask, text_query, text_key, text_value,
                                   scale=scale, return_lse=return_lse)
 
@@ -366,12 +432,23 @@ def lvsa_sdpa(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor, k_glo
               v_global: torch.Tensor, metadata: LVSAMetadata, attention_backend: Any = None) -> torch.Tensor:
     """Drop-in for lvsa_sdpa (lvsa/sparse_attention.py:643-706).
 
+    ``metadata`` is this package's LVSAMetadata or the reference's own
+    object (read through ``pattern_key``; its GPU mask is cached by pattern).
     query/key/value [B, S, H(kv), D]; k_global/v_global the gathered anchor
     K/V with any text K/V appended after them, as the processor builds them
-    (lvsa/lvsa_processor.py:545-549).  Anchor K/V are read in place from
-    ``key``/``value`` (identical at world = 1); only the appended text part of
-    k_global/v_global is used.  ``attention_backend`` is accepted and ignored.
+    (lvsa/lvsa_processor.py:545-549).  At world = 1 the anchor K/V are read
+    in place from ``key``/``value`` (identical there) and only the appended
+    text part of k_global/v_global is used.  For a rank's shard (world > 1)
+    the query, key and value are the local shard and k_global/v_global the
+    all-reduced [globals; text] buffer, as in the reference: the video rows
+    run as the video launch of the reference's context-parallel pattern.
+    ``attention_backend`` is accepted and ignored.
     """
+    if metadata.world > 1:
+        nt = _text_part(k_global, metadata)
+        pat = shard_pattern_for(metadata, query.device, nt)
+        out, _ = block_sparse_attention(query, key, value, pat.video, None, k_global, v_global)
+        return out
     nt = _text_part(k_global, metadata)
     tk = k_global[:, k_global.shape[1] - nt:] if nt else None
     tv = v_global[:, v_global.shape[1] - nt:] if nt else None

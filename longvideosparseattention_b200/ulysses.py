@@ -330,10 +330,11 @@ def ulysses_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, sizes: 
 def kernel_local_attention(metadata, scale: Optional[float] = None) -> Callable:
     """The default local step: the sm_100a kernel with the world = 1 mask."""
     from .block_sparse import block_sparse_attention
+    from .sparse_attention import mask_for
 
     def run(q, k, v, tq, tk, tv, q_tiles, out, text_out):
         nt = 0 if tk is None else int(tk.shape[1])
-        mask = metadata.block_mask(q.device, nt)
+        mask = mask_for(metadata, q.device, nt)
         block_sparse_attention(q, k, v, mask, tq, tk, tv, scale=scale, out=out, text_out=text_out,
                                q_tiles=q_tiles)
     return run
