@@ -55,6 +55,11 @@ typedef struct LvsaPattern {
   int32_t block_k;            /* key tile columns (multiple of 16, <= 256)  */
   int32_t n_guards;           /* extra global frames (boundary guards)      */
   const int32_t* guards;      /* HOST array of n_guards frame indices       */
+  /* Optional DEVICE int32 (ABI 102): the denoising step index.  When set,
+   * the builder reads it on the GPU and uses step % key_frame_interval as
+   * the keyframe offset (keyframe_offset is then ignored), so a captured
+   * CUDA graph or a shared mask rotates by updating one device word. */
+  const int32_t* device_step;
 } LvsaPattern;
 
 /* Sizes of every output of lvsa_build_mask for a pattern. */

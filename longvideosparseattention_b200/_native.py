@@ -40,7 +40,7 @@ class LvsaPattern(ctypes.Structure):
     _fields_ = [("total_frames", _i32), ("num_patches", _i32), ("window_size", _i32),
                 ("n_first_frames", _i32), ("key_frame_interval", _i32), ("keyframe_offset", _i32),
                 ("expand_window", _i32), ("n_text", _i32), ("block_q", _i32), ("block_k", _i32),
-                ("n_guards", _i32), ("guards", ctypes.POINTER(_i32))]
+                ("n_guards", _i32), ("guards", ctypes.POINTER(_i32)), ("device_step", _vp)]
 
 
 class LvsaMaskLayout(ctypes.Structure):

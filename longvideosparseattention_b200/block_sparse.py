@@ -101,14 +101,16 @@ class BlockMask:
 def mask_layout(total_frames: int, num_patches: int, window_size: int, n_first_frames: int,
                 key_frame_interval: Optional[int], keyframe_offset: int = 0,
                 expand_window: bool = True, n_text: int = 0, block_q: int = ATTN_BLOCK_Q,
-                block_k: int = ATTN_BLOCK_K, boundary_guards: Optional[Sequence[int]] = None):
+                block_k: int = ATTN_BLOCK_K, boundary_guards: Optional[Sequence[int]] = None,
+                device_step: Optional[torch.Tensor] = None):
     lib = N.load()
     guards = list(boundary_guards or [])
     garr = (ctypes.c_int32 * max(1, len(guards)))(*guards)
     pat = N.LvsaPattern(int(total_frames), int(num_patches), int(window_size), int(n_first_frames),
                         int(key_frame_interval or 0), int(keyframe_offset), int(bool(expand_window)),
                         int(n_text), int(block_q), int(block_k), len(guards),
-                        ctypes.cast(garr, ctypes.POINTER(ctypes.c_int32)))
+                        ctypes.cast(garr, ctypes.POINTER(ctypes.c_int32)),
+                        device_step.data_ptr() if device_step is not None else None)
     lay = N.LvsaMaskLayout()
     N.check(lib.lvsa_mask_layout(ctypes.byref(pat), ctypes.byref(lay)), "lvsa_mask_layout")
     return pat, lay, garr
@@ -119,14 +121,21 @@ def build_block_mask(total_frames: int, num_patches: int, window_size: int, n_fi
                      expand_window: bool = True, n_text: int = 0, block_q: int = ATTN_BLOCK_Q,
                      block_k: int = ATTN_BLOCK_K, boundary_guards: Optional[Sequence[int]] = None,
                      device: Optional[torch.device] = None,
-                     reuse: Optional[BlockMask] = None) -> BlockMask:
+                     reuse: Optional[BlockMask] = None,
+                     device_step: Optional[torch.Tensor] = None) -> BlockMask:
     """Build the step's pattern on the GPU (4 small kernels, no host sync).
 
     ``reuse``: a BlockMask of the same geometry whose buffers are overwritten
-    (per-step keyframe rotation without reallocation)."""
+    (per-step keyframe rotation without reallocation).  ``device_step``: a
+    one-element int32 CUDA tensor holding the step index; the builder reads
+    it on the GPU (keyframe offset = step mod key_frame_interval) and
+    ``keyframe_offset`` is ignored, so rotating is a device-side update of
+    that word (graph-replayable)."""
+    if device_step is not None and (not device_step.is_cuda or device_step.dtype != torch.int32):
+        raise ValueError("device_step must be a CUDA int32 tensor")
     pat, lay, _keep = mask_layout(total_frames, num_patches, window_size, n_first_frames,
                                   key_frame_interval, keyframe_offset, expand_window, n_text,
-                                  block_q, block_k, boundary_guards)
+                                  block_q, block_k, boundary_guards, device_step)
     device = torch.device(device) if device is not None else torch.device("cuda")
     if device.type != "cuda":
         raise RuntimeError("build_block_mask needs a CUDA device (no CPU fallback)")

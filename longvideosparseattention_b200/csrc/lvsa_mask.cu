@@ -23,6 +23,7 @@ constexpr int kMaxWords = LVSA_MAX_FRAMES / 32;
 
 struct FrameParams {
   int T, P, W, n_first, kfi, offset, expand, words;
+  const int32_t* step;  // device step index (offset = step mod kfi), or null
   uint32_t guard_bits[kMaxWords];
 };
 
@@ -58,8 +59,9 @@ __global__ void __launch_bounds__(1024) frame_pattern_kernel(FrameParams prm, Lv
   for (int i = tid; i < min(prm.n_first, T); i += nt) atomicOr(&gbits[i >> 5], 1u << (i & 31));
   if (prm.kfi > 0) {
     const int nk = (T + prm.kfi - 1) / prm.kfi;
+    const int off = prm.step ? ((*prm.step % prm.kfi) + prm.kfi) % prm.kfi : prm.offset;
     for (int i = tid; i < nk; i += nt) {
-      long long x = static_cast<long long>(prm.offset) + static_cast<long long>(i) * prm.kfi;
+      long long x = static_cast<long long>(off) + static_cast<long long>(i) * prm.kfi;
       int g = static_cast<int>(((x % T) + T) % T);  // Python modulo
       atomicOr(&gbits[g >> 5], 1u << (g & 31));
     }
@@ -331,6 +333,7 @@ extern "C" int lvsa_build_mask(const LvsaPattern* p, const LvsaMaskBuffers* out,
   fp.T = p->total_frames; fp.P = p->num_patches; fp.W = p->window_size;
   fp.n_first = p->n_first_frames; fp.kfi = p->key_frame_interval; fp.offset = p->keyframe_offset;
   fp.expand = p->expand_window ? 1 : 0; fp.words = L.frame_words;
+  fp.step = p->device_step;
   for (int i = 0; i < p->n_guards; ++i) fp.guard_bits[p->guards[i] >> 5] |= 1u << (p->guards[i] & 31);
   frame_pattern_kernel<<<1, 1024, 0, s>>>(fp, *out);
 

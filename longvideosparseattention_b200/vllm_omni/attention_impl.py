@@ -2,8 +2,8 @@
 
 ``forward_cuda(q, k, v)`` receives the joint ``[video; text]`` sequence of a
 layer.  It detects the frame geometry from the sequence length
-(``seq_len = T_lat * P + text``), rebuilds the step's pattern when T/P change
-or keyframes rotate, and runs the video rows (sparse, plus all text) and the
+(``seq_len = T_lat * P + text``), reads the step's pattern (rebuilt on the
+GPU when T/P change or keyframes rotate), and runs the video rows (sparse, plus all text) and the
 text rows (dense) in ONE launch of the sm_100a kernel.  Cross-attention and
 non-frame sequences use the model's dense attention, as the reference does.
 """
@@ -15,6 +15,7 @@ import torch.nn.functional as F
 
 from ..block_sparse import block_sparse_attention
 from ..sparse_attention import LVSAMetadata, compute_auto_kfi
+from ..step_mask import SHARED
 from . import step_tracker
 from ._fallback import warn_fallback
 from .config import LVSAConfig, candidate_patches_per_frame
@@ -68,7 +69,21 @@ class LVSAAttentionImpl:
                 return p, text
         return None, None
 
+    def _mask(self, T: int, P: int, text: int, device: torch.device):
+        """The step's GPU mask, one per pattern for all instances
+        (``step_mask.SHARED``; rebuilt in place once per rotation, no host
+        metadata build)."""
+        cfg = self.config
+        W, nf = cfg.latent_window_size, cfg.latent_n_first_frames
+        kfi = cfg.latent_key_frame_interval
+        if cfg.auto_keyframes:
+            kfi = compute_auto_kfi(T, W, nf, cfg.reference_latent_frames, cfg.sparsity_scale)
+        return SHARED.get(device, T, P, W, nf, kfi, cfg.expand_window, text, step_tracker.get_step(),
+                          rotate=cfg.rotate_keyframes)
+
     def _metadata(self, T: int, P: int) -> LVSAMetadata:
+        """Host LVSAMetadata of the current step (reference interface; the
+        forward path uses ``_mask``)."""
         cfg = self.config
         W, nf = cfg.latent_window_size, cfg.latent_n_first_frames
         kfi = cfg.latent_key_frame_interval
@@ -99,7 +114,7 @@ class LVSAAttentionImpl:
         if P is None:
             warn_fallback("forward_cuda", "geometry_detect", query.shape[1], {"T_lat": T})
             return self._dense_attention(query, key, value)
-        meta = self._metadata(T, P)
+        mask = self._mask(T, P, text, query.device)
         nv = T * P
         tq = query[:, nv:] if text else None
         tk = key[:, nv:] if text else None
@@ -107,6 +122,6 @@ class LVSAAttentionImpl:
         out = torch.empty_like(query)
         o_v = out[:, :nv]
         o_t = out[:, nv:] if text else None
-        res = block_sparse_attention(query[:, :nv], key[:, :nv], value[:, :nv], meta.block_mask(query.device, text),
-                                     tq, tk, tv, scale=self.softmax_scale, out=o_v, text_out=o_t)
+        block_sparse_attention(query[:, :nv], key[:, :nv], value[:, :nv], mask, tq, tk, tv,
+                               scale=self.softmax_scale, out=o_v, text_out=o_t)
         return out

@@ -47,15 +47,15 @@ def install_cosmos3_lvsa_hook(total_latent_frames: int) -> None:
         q = F.rms_norm(q, (q.shape[-1],), self.norm_q.weight, self.norm_q.variance_epsilon)
         k = F.rms_norm(k, (k.shape[-1],), self.norm_k.weight, self.norm_k.variance_epsilon)
         q, k = _apply_rotary_pos_emb(q, k, freqs_cos, freqs_sin)
-        meta = state.get_metadata(total_latent_frames, P, step_idx, q.device)
-        _log_engagement_once(state, "cosmos3", total_latent_frames, P, S_gen, meta)
-        _maybe_log_mask(state, step_idx, total_latent_frames, meta)
+        _log_engagement_once(state, "cosmos3", total_latent_frames, P, S_gen, step_idx)
+        _maybe_log_mask(state, step_idx, total_latent_frames)
         if repeat_kv and self.num_heads_local != self.num_kv_heads_local:
             rep = self.num_heads_local // self.num_kv_heads_local
             k, v = k.repeat_interleave(rep, dim=2), v.repeat_interleave(rep, dim=2)
             k_und, v_und = k_und.repeat_interleave(rep, dim=2), v_und.repeat_interleave(rep, dim=2)
         # Generation rows: sparse pattern + every understanding token (no text query rows).
-        out, _ = block_sparse_attention(q, k, v, meta.block_mask(q.device, int(k_und.shape[1])), None, k_und, v_und)
+        mask = state.get_mask(total_latent_frames, P, step_idx, q.device, int(k_und.shape[1]))
+        out, _ = block_sparse_attention(q, k, v, mask, None, k_und, v_und)
         return self.to_out(out.reshape(B, S_gen, -1))
 
     Cosmos3CrossAttention.forward = _lvsa_forward

@@ -10,12 +10,15 @@ text queries.  vllm-omni is imported only when a hook is installed.
 """
 
 import os
+from types import SimpleNamespace
 from typing import Optional
 
 import torch
 
 from ..block_sparse import block_sparse_attention
-from ..sparse_attention import LVSAMetadata, compute_auto_kfi, print_attention_mask_compact
+from ..sparse_attention import LVSAMetadata, compute_auto_kfi, compute_global_indices, \
+    print_attention_mask_compact
+from ..step_mask import SHARED
 from ._fallback import warn_fallback
 from .config import LVSAConfig
 
@@ -38,21 +41,23 @@ def _mask_log_should_fire(spec: str, step_idx: int, last_step: int) -> bool:
         return False
 
 
-def _log_engagement_once(state, model, total_latent_frames, num_patches, seq_len, metadata) -> None:
+def _log_engagement_once(state, model, total_latent_frames, num_patches, seq_len, step_idx) -> None:
     """One line per generation confirming that the sparse path engaged."""
     if state._engaged_logged:
         return
     state._engaged_logged = True
+    metadata = state.pattern_info(total_latent_frames, step_idx)
     kfi = metadata.key_frame_interval
     mode = "SPARSE" if kfi > 1 else "DENSE (T_lat <= ref)"
     print(f"[LVSA] engaged ({model}): T_lat={total_latent_frames} P={num_patches} seq_len={seq_len} "
           f"kfi={kfi} W={metadata.window_size} |G|={len(metadata.global_set)} -> {mode}", flush=True)
 
 
-def _maybe_log_mask(state, step_idx: int, total_latent_frames: int, metadata) -> None:
+def _maybe_log_mask(state, step_idx: int, total_latent_frames: int) -> None:
     spec = os.environ.get("LVSA_MASK_LOG", "")
     if _mask_log_should_fire(spec, step_idx, state._mask_log_last_step):
         state._mask_log_last_step = step_idx
+        metadata = state.pattern_info(total_latent_frames, step_idx)
         print(f"[LVSA-MASK] step={step_idx}  T_lat={total_latent_frames}  W={metadata.window_size}  "
               f"|G|={len(metadata.global_set)}  kfi={metadata.key_frame_interval}", flush=True)
         print_attention_mask_compact(total_latent_frames, metadata.window_size, metadata.global_set,
@@ -108,8 +113,39 @@ class HunyuanLVSAState:
             self._step = max(self._step, (self._call_count - 1) // (self._n_blocks * self._cfg_passes))
         return self._step
 
+    def key_frame_interval(self, total_latent_frames: int) -> Optional[int]:
+        cfg = self.config
+        kfi = cfg.latent_key_frame_interval
+        if cfg.auto_keyframes:
+            kfi = compute_auto_kfi(total_latent_frames, cfg.latent_window_size, cfg.latent_n_first_frames,
+                                   reference_frames=cfg.reference_latent_frames,
+                                   sparsity_scale=cfg.sparsity_scale)
+        return kfi
+
+    def pattern_info(self, total_latent_frames: int, step_idx: int) -> SimpleNamespace:
+        """The fields the engagement and mask logs print (host arithmetic
+        only: the global frame list, no metadata build)."""
+        cfg = self.config
+        kfi = self.key_frame_interval(total_latent_frames)
+        off = step_idx % kfi if (cfg.rotate_keyframes and kfi and kfi > 0) else 0
+        g = compute_global_indices(total_latent_frames, cfg.latent_n_first_frames, kfi, off)
+        return SimpleNamespace(key_frame_interval=kfi, window_size=cfg.latent_window_size,
+                               global_set=set(g), global_indices=g, expand_window=True)
+
+    def get_mask(self, total_latent_frames: int, num_patches: int, step_idx: int, device: torch.device,
+                 n_text: int = 0):
+        """The step's GPU block mask, shared with every other hooked block and
+        impl instance (``step_mask.SHARED``): built once per rotation into
+        the same buffers, keyframe offset read on the GPU from the step."""
+        cfg = self.config
+        return SHARED.get(device, total_latent_frames, num_patches, cfg.latent_window_size,
+                          cfg.latent_n_first_frames, self.key_frame_interval(total_latent_frames), True,
+                          n_text, step_idx, rotate=cfg.rotate_keyframes)
+
     def get_metadata(self, total_latent_frames: int, num_patches: int, step_idx: int,
                      device: torch.device) -> LVSAMetadata:
+        """Host LVSAMetadata of the step (reference interface; the forward
+        path uses ``get_mask`` and never builds this)."""
         cfg = self.config
         if (self._metadata is None or self._cached_total_frames != total_latent_frames
                 or self._cached_patches != num_patches or (cfg.rotate_keyframes and self._cached_step != step_idx)):
@@ -122,7 +158,6 @@ class HunyuanLVSAState:
                                                 expand_window=True, keyframe_offset=offset,
                                                 reference_frames=cfg.reference_latent_frames,
                                                 sparsity_scale=cfg.sparsity_scale)
-            self._metadata.ensure_device(device)
             self._cached_total_frames, self._cached_patches, self._cached_step = (
                 total_latent_frames, num_patches, step_idx)
         return self._metadata
@@ -165,11 +200,11 @@ def install_hunyuan_lvsa_hook(total_latent_frames: int) -> None:
         eq, ek, ev = eqkv.split([enh * hd, enkv * hd, enkv * hd], dim=-1)
         eq, ek, ev = eq.unflatten(-1, (enh, -1)), ek.unflatten(-1, (enkv, -1)), ev.unflatten(-1, (enkv, -1))
         eq, ek = self.norm_added_q(eq), self.norm_added_k(ek)
-        meta = state.get_metadata(total_latent_frames, P, step_idx, q.device)
-        _log_engagement_once(state, "hunyuan", total_latent_frames, P, video_seq, meta)
-        _maybe_log_mask(state, step_idx, total_latent_frames, meta)
+        _log_engagement_once(state, "hunyuan", total_latent_frames, P, video_seq, step_idx)
+        _maybe_log_mask(state, step_idx, total_latent_frames)
+        mask = state.get_mask(total_latent_frames, P, step_idx, q.device, int(ek.shape[1]))
         # Video rows sparse + every text token, text rows dense: one launch.
-        out, enc_out = block_sparse_attention(q, k, v, meta.block_mask(q.device, int(ek.shape[1])), eq, ek, ev)
+        out, enc_out = block_sparse_attention(q, k, v, mask, eq, ek, ev)
         hs = self.to_out[0](out.flatten(2, 3).to(q.dtype))
         enc = self.to_add_out(enc_out.flatten(2, 3).to(q.dtype))
         return hs, enc

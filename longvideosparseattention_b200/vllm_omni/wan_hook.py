@@ -40,10 +40,9 @@ def install_wan_lvsa_hook(total_latent_frames: int) -> None:
         if rotary_emb is not None:
             cos, sin = rotary_emb
             q, k = wan_rope(q, cos, sin), wan_rope(k, cos, sin)
-        meta = state.get_metadata(total_latent_frames, P, step_idx, q.device)
-        _log_engagement_once(state, "wan", total_latent_frames, P, seq, meta)
-        _maybe_log_mask(state, step_idx, total_latent_frames, meta)
-        out, _ = block_sparse_attention(q, k, v, meta.block_mask(q.device, 0))
+        _log_engagement_once(state, "wan", total_latent_frames, P, seq, step_idx)
+        _maybe_log_mask(state, step_idx, total_latent_frames)
+        out, _ = block_sparse_attention(q, k, v, state.get_mask(total_latent_frames, P, step_idx, q.device, 0))
         out = self.to_out(out.flatten(2, 3).type_as(q))
         return self.dropout(out)
 
