@@ -18,7 +18,7 @@ T, P, H, D, NT = 13, 200, 2, 128, 40
 
 @pytest.fixture
 def plugin_env(monkeypatch):
-    for k, v in dict(LVSA_WINDOW_SIZE="1", LVSA_N_FIRST_FRAMES="1", LVSA_KEY_FRAME_INTERVAL="4",
+    for k, v in dict(LVSA_WINDOW_SIZE="4", LVSA_N_FIRST_FRAMES="4", LVSA_KEY_FRAME_INTERVAL="16",  # video frames (/4)
                      LVSA_AUTO_KEYFRAMES="0", LVSA_ROTATE_KEYFRAMES="1", LVSA_TOTAL_LATENT_FRAMES=str(T),
                      LVSA_PATCHES_PER_FRAME=str(P)).items():
         monkeypatch.setenv(k, v)
