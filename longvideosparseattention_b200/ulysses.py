@@ -180,6 +180,14 @@ def _video_rows(p: Piece, n_q_video_tiles: int, n_video: int) -> Tuple[int, int]
 
 
 _SCHED_CACHE: Dict[tuple, UlyssesSchedule] = {}
+_STREAMS: Dict[tuple, List[torch.cuda.Stream]] = {}
+
+
+def _piece_streams(device: torch.device, n: int) -> List[torch.cuda.Stream]:
+    key = (str(device), n)
+    if key not in _STREAMS:
+        _STREAMS[key] = [torch.cuda.Stream(device=device) for _ in range(n)]
+    return _STREAMS[key]
 
 
 def ulysses_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, sizes: Sequence[int],
@@ -261,14 +269,34 @@ def ulysses_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, sizes: 
     # ---- local attention, one launch per piece
     out_loc = torch.empty(B, S, max(nqh, 1), D, dtype=dt, device=dev)
     tout_loc = torch.zeros(B, Nt, max(nqh, 1), D, dtype=dt, device=dev) if text_rows else None
-    for p in sch.pieces[rank]:
+    pieces = sch.pieces[rank]
+    # Several pieces (a partial head beside whole heads): launch them on
+    # concurrent streams, so the CTAs of one fill the last wave of another.
+    streams = _piece_streams(dev, len(pieces)) if (q.is_cuda and len(pieces) > 1) else None
+    if streams:
+        cur = torch.cuda.current_stream(dev)
+        for st in streams:
+            st.wait_stream(cur)
+    for j, p in enumerate(pieces):
         hq = slice(p.h0 - qa, p.h1 - qa)
         hk = slice(p.h0 // g - ka, (p.h1 - 1) // g + 1 - ka)
         tq = text_q[:, :, p.h0:p.h1] if text_rows else None
         tk = text_k[:, :, p.h0 // g:(p.h1 - 1) // g + 1] if Nt else None
         tv = text_v[:, :, p.h0 // g:(p.h1 - 1) // g + 1] if Nt else None
-        local_attention(qf[:, :, hq], kf[:, :, hk], vf[:, :, hk], tq, tk, tv, (p.t0, p.t1),
-                        out_loc[:, :, hq], tout_loc[:, :, hq] if text_rows else None)
+        args = (qf[:, :, hq], kf[:, :, hk], vf[:, :, hk], tq, tk, tv, (p.t0, p.t1),
+                out_loc[:, :, hq], tout_loc[:, :, hq] if text_rows else None)
+        if streams:
+            with torch.cuda.stream(streams[j]):
+                local_attention(*args)
+        else:
+            local_attention(*args)
+    if streams:
+        for st in streams:
+            cur.wait_stream(st)
+        for t in (x, out_loc, tout_loc):
+            if t is not None:
+                for st in streams:
+                    t.record_stream(st)
     ev("attended")
 
     # ---- return: the video rows of my pieces to their token owners

@@ -6,7 +6,6 @@ slicing, which the gloo test shows equals the all-reduce); a 2-GPU NCCL run
 checks the collective path."""
 
 import os
-import socket
 
 import numpy as np
 import pytest
@@ -57,20 +56,13 @@ def test_cp_ranks_match_reference(name):
             _cmp(tout, CP[f"{name}.text_out{r}"])
 
 
-def _port():
-    s = socket.socket()
-    s.bind(("127.0.0.1", 0))
-    p = s.getsockname()[1]
-    s.close()
-    return p
-
-
 def _worker(rank, world, port, out_dir):
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    os.environ.update(NCCL_NVLS_ENABLE="0")
     import torch.distributed as dist
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
-    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
+    # File rendezvous: no TCP port to race for between back-to-back tests.
+    dist.init_process_group("nccl", init_method="file://" + port, rank=rank, world_size=world, device_id=dev)
     try:
         from longvideosparseattention_b200.cp_mode import GlobalKV, build_shard_pattern, cp_attention
         name = "cp_w2"
@@ -90,7 +82,7 @@ def _worker(rank, world, port, out_dir):
 def test_cp_two_gpus_nccl(tmp_path):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
-    mp.spawn(_worker, args=(2, _port(), str(tmp_path)), nprocs=2, join=True)
+    mp.spawn(_worker, args=(2, os.path.join(str(tmp_path), "rdzv"), str(tmp_path)), nprocs=2, join=True)
     for r in range(2):
         res = torch.load(os.path.join(tmp_path, f"r{r}.pt"))
         _cmp(res["out"], CP[f"cp_w2.out{r}"])

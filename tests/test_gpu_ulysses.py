@@ -6,21 +6,12 @@ ranks' schedules emulated one after another).  The multi-GPU cases skip with
 fewer than 2 GPUs."""
 
 import os
-import socket
 
 import pytest
 import torch
 import torch.multiprocessing as mp
 
 pytestmark = pytest.mark.gpu
-
-
-def _port():
-    s = socket.socket()
-    s.bind(("127.0.0.1", 0))
-    p = s.getsockname()[1]
-    s.close()
-    return p
 
 
 CASES = [dict(T=9, P=230, H=4, Hkv=4, D=128, W=1, kfi=4, off=1, nt=40),
@@ -38,11 +29,12 @@ def _inputs(device, c):
 
 
 def _worker(rank, world, port, out_dir, c):
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    os.environ.update(NCCL_NVLS_ENABLE="0")
     import torch.distributed as dist
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
-    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
+    # File rendezvous: no TCP port to race for between back-to-back tests.
+    dist.init_process_group("nccl", init_method="file://" + port, rank=rank, world_size=world, device_id=dev)
     try:
         from longvideosparseattention_b200 import build_block_mask
         from longvideosparseattention_b200.ulysses import mask_local_attention, shard_sizes, tile_costs, \
@@ -109,7 +101,7 @@ def test_ulysses_multi_gpu_match_single_gpu(tmp_path, ci, world):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     c = CASES[ci]
-    mp.spawn(_worker, args=(world, _port(), str(tmp_path), c), nprocs=world, join=True)
+    mp.spawn(_worker, args=(world, os.path.join(str(tmp_path), "rdzv"), str(tmp_path), c), nprocs=world, join=True)
     ref, tref = _single_gpu(c, torch.device("cuda", 0))
     got = torch.cat([torch.load(tmp_path / f"r{r}.pt")["out"] for r in range(world)], dim=1)
     assert torch.equal(got, ref.cpu())  # same kernel on the same per-head rows: bitwise
