@@ -137,6 +137,14 @@ typedef struct LvsaAttnArgs {
    * head under head-and-tile partitioned Ulysses parallelism.  Rows outside
    * the range (and their LSE entries) are not written. */
   int32_t end_q_tile;
+  /* Limit of every bounded wait inside the kernel, in microseconds (ABI
+   * 102); <= 0: 2 s.  On expiry the CTA records LVSA_ERR_DEVICE_TIMEOUT in
+   * *error_word, drains its own copies and MMAs, frees its tensor memory and
+   * returns; the context stays usable. */
+  int32_t wait_timeout_us;
+  /* Test hook (0 in normal use): 1 makes CTA (0, 0, 0) skip its query-tile
+   * load, so its waits expire and the path above runs. */
+  int32_t inject_fault;
 } LvsaAttnArgs;
 
 /* Block-sparse attention forward on tcgen05/TMEM, K/V read in place.

@@ -229,7 +229,8 @@ def block_sparse_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, ma
                            scale: Optional[float] = None, return_lse: bool = False,
                            out: Optional[torch.Tensor] = None,
                            text_out: Optional[torch.Tensor] = None, fp8: bool = False,
-                           q_tiles: Optional[Tuple[int, int]] = None):
+                           q_tiles: Optional[Tuple[int, int]] = None, wait_timeout_us: int = 0,
+                           inject_fault: int = 0):
     """LVSA attention of one layer on the GPU.
 
     q [B, Nv, H, D], k/v [B, Nv, Hkv, D] (video, frame-major tokens);
@@ -242,6 +243,10 @@ def block_sparse_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, ma
     ``q_tiles=(t0, t1)`` computes only tile-CSR rows [t0, t1) (video rows
     first, then text rows); the other rows of ``out`` / ``text_out`` are
     left as they are, so pass them to keep their contents.
+
+    ``wait_timeout_us`` bounds every wait inside the kernel (default 2 s);
+    ``inject_fault=1`` is a test hook that makes one CTA's waits expire
+    (its rows are not written; the device error word reports it).
     """
     if not q.is_cuda:
         raise RuntimeError("block_sparse_attention needs CUDA tensors (no CPU fallback)")
@@ -295,7 +300,7 @@ def block_sparse_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, ma
         mask.tile_flags.data_ptr(), error_word(q.device).data_ptr(),
         getattr(mask, "token_offset", 0),
         int(q_tiles[0]) if q_tiles is not None else getattr(mask, "first_q_tile", 0),
-        int(q_tiles[1]) if q_tiles is not None else 0)
+        int(q_tiles[1]) if q_tiles is not None else 0, int(wait_timeout_us), int(inject_fault))
     with torch.cuda.device(q.device):
         if fp8:
             st = N.load().lvsa_attn_fwd_fp8(ctypes.byref(args), ctypes.byref(sc_c), _stream_ptr(q.device))

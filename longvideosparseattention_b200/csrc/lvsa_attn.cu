@@ -97,6 +97,8 @@ struct AttnParams {
   // Tile-pair kernel: video rows [row0, pair_ve) in pair_nv pairs, then text
   // rows [pair_ts, pair_end).
   int pair_ve, pair_ts, pair_end, pair_nv;
+  uint64_t wait_ns;  // limit of every bounded wait
+  int inject;        // test hook: CTA (0, 0, 0) never loads its query tile
 };
 
 
@@ -340,9 +342,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_prefetch_desc(mq);
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
-      mbar_expect_tx(q_full, L::kTile);
+      const bool skip_q = prm.inject && (blockIdx.x | blockIdx.y | blockIdx.z) == 0;
+      if (!skip_q) {
+        mbar_expect_tx(q_full, L::kTile);
 #pragma unroll
-      for (int c = 0; c < L::kCh; ++c) tma_load_4d(sQ + c * kChunk, mq, q_full, c * (128 / L::kElem), h, tok0, b);
+        for (int c = 0; c < L::kCh; ++c) tma_load_4d(sQ + c * kChunk, mq, q_full, c * (128 / L::kElem), h, tok0, b);
+      }
       int k_issued = 0, v_issued = 0;
       for (int j = 0; j < n; ++j) {
         const int s = j % SK, sv = j % SV;
@@ -351,14 +356,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int ktok = (tt ? kt - prm.nkv : kt) * kBN;
         const CUtensorMap* mk = tt ? &tm_tk : &tm_k;
         const CUtensorMap* mv = tt ? &tm_tv : &tm_v;
-        if (j >= SK && !mbar_wait(&k_empty[s], ((j / SK) - 1) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT))
+        if (j >= SK && !mbar_wait(&k_empty[s], ((j / SK) - 1) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT, prm.wait_ns))
           break;
         mbar_expect_tx(&k_full[s], L::kTile);
 #pragma unroll
         for (int c = 0; c < L::kCh; ++c)
           tma_load_4d(sK + s * L::kTile + c * kChunk, mk, &k_full[s], c * (128 / L::kElem), hk, ktok, b);
         k_issued = j + 1;
-        if (j >= SV && !mbar_wait(&v_empty[sv], ((j / SV) - 1) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT))
+        if (j >= SV && !mbar_wait(&v_empty[sv], ((j / SV) - 1) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT, prm.wait_ns))
           break;
         mbar_expect_tx(&v_full[sv], L::kTile);
 #pragma unroll
@@ -368,7 +373,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (*abort) {
         // Drain our own copies still in flight before the CTA retires.
-        mbar_wait(q_full, 0, never, nullptr, 0);
+        if (!skip_q) mbar_wait(q_full, 0, never, nullptr, 0);
         for (int j = max(0, k_issued - SK); j < k_issued; ++j)
           mbar_wait(&k_full[j % SK], (j / SK) & 1, never, nullptr, 0);
         for (int j = max(0, v_issued - SV); j < v_issued; ++j)
@@ -394,21 +399,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         mma_commit(&s_full[jj & 1]);
         mma_commit(&k_empty[jj % SK]);
       };
-      bool ok = mbar_wait(q_full, 0, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT) &&
-                mbar_wait(&k_full[0], 0, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT);
+      bool ok = mbar_wait(q_full, 0, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT, prm.wait_ns) &&
+                mbar_wait(&k_full[0], 0, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT, prm.wait_ns);
       if (ok) {
         tc_fence_after();
         issue_s(0);
       }
       if (ok && n > 1 && (ok = mbar_wait(&k_full[1 % SK], (1 / SK) & 1, abort, prm.err,
-                                         LVSA_ERR_DEVICE_TIMEOUT))) {
+                                         LVSA_ERR_DEVICE_TIMEOUT, prm.wait_ns))) {
         tc_fence_after();
         issue_s(1);
       }
       for (int j = 0; ok && j < n; ++j) {
         const int c = j & 1, it = j >> 1;
-        if (!(ok = mbar_wait(&p_full[c], it & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT))) break;
-        if (!(ok = mbar_wait(&v_full[j % SV], (j / SV) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT))) break;
+        if (!(ok = mbar_wait(&p_full[c], it & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT, prm.wait_ns))) break;
+        if (!(ok = mbar_wait(&v_full[j % SV], (j / SV) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT, prm.wait_ns))) break;
         tc_fence_after();
         const uint32_t vb = v_base + (j % SV) * L::kTile, pa = tS + c * 128, dO = tO + c * 128;
 #pragma unroll
@@ -419,7 +424,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (j + 2 < n) {
           // S buffer c: P(j) was read by PV(j), issued just before.
           if (!(ok = mbar_wait(&k_full[(j + 2) % SK], ((j + 2) / SK) & 1, abort, prm.err,
-                               LVSA_ERR_DEVICE_TIMEOUT)))
+                               LVSA_ERR_DEVICE_TIMEOUT, prm.wait_ns)))
             break;
           tc_fence_after();
           issue_s(j + 2);
@@ -471,7 +476,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       uint32_t am[4] = {~0u, ~0u, ~0u, ~0u};
       if (flag) tile_mask(am, prm, kt, text_row, fbits);
-      if (!__all_sync(0xFFFFFFFFu, mbar_wait(&s_full[cls], it & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT))) {
+      if (!__all_sync(0xFFFFFFFFu, mbar_wait(&s_full[cls], it & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT, prm.wait_ns))) {
         ok = false;
         break;
       }
@@ -538,7 +543,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (obase) obase += cls * (D / 2);
     if (n > 0) {
       const bool got =
-          ok && __all_sync(0xFFFFFFFFu, mbar_wait(o_done, 0, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT));
+          ok && __all_sync(0xFFFFFFFFu, mbar_wait(o_done, 0, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT, prm.wait_ns));
       // After o_done no MMA reads the query tile any more: reuse it.
       float* red_m = reinterpret_cast<float*>(sQ);   // [2 classes][128 rows]
       float* red_l = red_m + 2 * kBM;                // NaN marks a class that timed out
@@ -716,11 +721,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_prefetch_desc(mq);
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
-      mbar_expect_tx(q_full, (has_b ? 2 : 1) * L::kTile);
-      for (int t = 0; t < (has_b ? 2 : 1); ++t)
+      const bool skip_q = prm.inject && (blockIdx.x | blockIdx.y | blockIdx.z) == 0;
+      if (!skip_q) {
+        mbar_expect_tx(q_full, (has_b ? 2 : 1) * L::kTile);
+        for (int t = 0; t < (has_b ? 2 : 1); ++t)
 #pragma unroll
-        for (int c = 0; c < L::kCh; ++c)
-          tma_load_4d(sQ + t * L::kTile + c * kChunk, mq, q_full, c * (128 / L::kElem), h, tok_a + t * kBM, b);
+          for (int c = 0; c < L::kCh; ++c)
+            tma_load_4d(sQ + t * L::kTile + c * kChunk, mq, q_full, c * (128 / L::kElem), h, tok_a + t * kBM, b);
+      }
       int gc = 0, issued = 0;
       bool ok = true;
       for (int i = 0; ok && i < nmax; ++i) {
@@ -734,13 +742,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int ktok = (tt ? kt - prm.nkv : kt) * kBN;
           const CUtensorMap* mk = tt ? &tm_tk : &tm_k;
           const CUtensorMap* mv = tt ? &tm_tv : &tm_v;
-          if (g >= SK && !(ok = mbar_wait(&k_empty[s], ((g / SK) - 1) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT)))
+          if (g >= SK && !(ok = mbar_wait(&k_empty[s], ((g / SK) - 1) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT, prm.wait_ns)))
             break;
           mbar_expect_tx(&k_full[s], L::kTile);
 #pragma unroll
           for (int c = 0; c < L::kCh; ++c)
             tma_load_4d(sK + s * L::kTile + c * kChunk, mk, &k_full[s], c * (128 / L::kElem), hk, ktok, b);
-          if (g >= SV && !(ok = mbar_wait(&v_empty[sv], ((g / SV) - 1) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT))) {
+          if (g >= SV && !(ok = mbar_wait(&v_empty[sv], ((g / SV) - 1) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT, prm.wait_ns))) {
             issued = -(g + 1);  // K of load g issued, V not
             break;
           }
@@ -754,7 +762,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (*abort) {
         // Drain our own copies still in flight before the CTA retires.
         const int k_issued = issued < 0 ? -issued : issued, v_issued = issued < 0 ? -issued - 1 : issued;
-        mbar_wait(q_full, 0, never, nullptr, 0);
+        if (!skip_q) mbar_wait(q_full, 0, never, nullptr, 0);
         for (int g = max(0, k_issued - SK); g < k_issued; ++g)
           mbar_wait(&k_full[g % SK], (g / SK) & 1, never, nullptr, 0);
         for (int g = max(0, v_issued - SV); g < v_issued; ++g)
@@ -771,7 +779,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int nc[2] = {n0, n1};
       // S_c(i) from load g; `last`: no later S reads that K stage.
       auto issue_s = [&](int c, int g, bool last) -> bool {
-        if (!mbar_wait(&k_full[g % SK], (g / SK) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT)) return false;
+        if (!mbar_wait(&k_full[g % SK], (g / SK) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT, prm.wait_ns)) return false;
         tc_fence_after();
         const uint32_t kb = k_base + (g % SK) * L::kTile, qb = q_base + c * L::kTile, dS = tS + c * 128;
 #pragma unroll
@@ -784,8 +792,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         return true;
       };
       auto issue_pv = [&](int c, int i, int g, bool last) -> bool {
-        if (!mbar_wait(&p_full[c], i & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT)) return false;
-        if (!mbar_wait(&v_full[g % SV], (g / SV) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT)) return false;
+        if (!mbar_wait(&p_full[c], i & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT, prm.wait_ns)) return false;
+        if (!mbar_wait(&v_full[g % SV], (g / SV) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT, prm.wait_ns)) return false;
         tc_fence_after();
         const uint32_t vb = v_base + (g % SV) * L::kTile, pa = tS + c * 128, dO = tO + c * 128;
 #pragma unroll
@@ -795,7 +803,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (last) mma_commit(&v_empty[g % SV]);
         return true;
       };
-      bool ok = mbar_wait(q_full, 0, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT);
+      bool ok = mbar_wait(q_full, 0, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT, prm.wait_ns);
       int gc = 0;
       PairStep cur = pair_step(0, l0, n0, l1, n1, gc);
       if (ok && cur.g0 >= 0) ok = issue_s(0, cur.g0, !cur.shared);
@@ -862,7 +870,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       uint32_t am[4] = {~0u, ~0u, ~0u, ~0u};
       if (flag) tile_mask(am, prm, kt, text_row, fbits);
-      if (!__all_sync(0xFFFFFFFFu, mbar_wait(&s_full[cls], it & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT))) {
+      if (!__all_sync(0xFFFFFFFFu, mbar_wait(&s_full[cls], it & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT, prm.wait_ns))) {
         ok = false;
         break;
       }
@@ -924,7 +932,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (n > 0) {
       const bool got =
-          ok && __all_sync(0xFFFFFFFFu, mbar_wait(o_done, 0, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT));
+          ok && __all_sync(0xFFFFFFFFu, mbar_wait(o_done, 0, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT, prm.wait_ns));
       if (got) {
         tc_fence_after();
         const float inv = (l > 0.f) ? vref / l : 0.f;
@@ -1046,6 +1054,8 @@ int launch(const LvsaAttnArgs* a, cudaStream_t stream, const LvsaFp8Scales* sc =
   p.scale_log2 = scale * 1.4426950408889634f;
   p.frame_bits = a->frame_bits; p.indptr = a->tile_indptr; p.indices = a->tile_indices; p.flags = a->tile_flags;
   p.err = a->error_word;
+  p.wait_ns = a->wait_timeout_us > 0 ? static_cast<uint64_t>(a->wait_timeout_us) * 1000ull : kWaitTimeoutNs;
+  p.inject = a->inject_fault;
   p.qs = p.ks = p.vs = p.tqs = p.tks = p.tvs = p.vref = nullptr;
   p.nqt_all = (a->n_text + kBlockQ - 1) / kBlockQ;
   p.nkt = (a->n_text + kBN - 1) / kBN;

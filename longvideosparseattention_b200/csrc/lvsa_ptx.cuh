@@ -65,7 +65,7 @@ __device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
 constexpr uint64_t kWaitTimeoutNs = 2000000000ull;  // 2 s; a healthy wait is < 1 ms
 
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
-                                          int* err, int code) {
+                                          int* err, int code, uint64_t timeout_ns = kWaitTimeoutNs) {
   const uint32_t a = smem_u32(bar);
   if (mbar_try_wait(a, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
@@ -73,7 +73,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     if (mbar_try_wait(a, parity)) return true;
     if ((it & 255u) == 0) {
       if (*abort) return false;
-      if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+      if (globaltimer_ns() - t0 > timeout_ns) {
         *abort = 1;
         if (err) atomicCAS(err, 0, code);
         return false;

@@ -136,8 +136,9 @@ def test_struct_layouts_match_header():
 int main(void){
  printf("%zu %zu %zu %zu %zu\n", sizeof(LvsaPattern), sizeof(LvsaMaskLayout), sizeof(LvsaMaskBuffers),
         sizeof(LvsaTensor), sizeof(LvsaAttnArgs));
- printf("%zu %zu %zu %zu %zu\n", offsetof(LvsaAttnArgs, scale), offsetof(LvsaAttnArgs, frame_bits),
-        offsetof(LvsaAttnArgs, error_word), offsetof(LvsaAttnArgs, end_q_tile), sizeof(LvsaCopySegment));
+ printf("%zu %zu %zu %zu %zu %zu\n", offsetof(LvsaAttnArgs, scale), offsetof(LvsaAttnArgs, frame_bits),
+        offsetof(LvsaAttnArgs, error_word), offsetof(LvsaAttnArgs, end_q_tile), sizeof(LvsaCopySegment),
+        offsetof(LvsaAttnArgs, inject_fault));
  return 0;}
 '''
     import tempfile
@@ -152,7 +153,8 @@ int main(void){
     want = [ctypes.sizeof(N.LvsaPattern), ctypes.sizeof(N.LvsaMaskLayout),
             ctypes.sizeof(N.LvsaMaskBuffers), ctypes.sizeof(N.LvsaTensor), ctypes.sizeof(N.LvsaAttnArgs),
             N.LvsaAttnArgs.scale.offset, N.LvsaAttnArgs.frame_bits.offset, N.LvsaAttnArgs.error_word.offset,
-            N.LvsaAttnArgs.end_q_tile.offset, ctypes.sizeof(N.LvsaCopySegment)]
+            N.LvsaAttnArgs.end_q_tile.offset, ctypes.sizeof(N.LvsaCopySegment),
+            N.LvsaAttnArgs.inject_fault.offset]
     assert got == want
 
 
