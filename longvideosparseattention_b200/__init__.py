@@ -9,3 +9,4 @@ __version__ = "0.1.0"
 
 from .block_sparse import (BlockMask, block_sparse_attention, build_block_mask,  # noqa: F401
                            check_device_errors, mask_layout)
+from .observability import lvsa_stats, memory_stats  # noqa: F401,E402

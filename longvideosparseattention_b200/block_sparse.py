@@ -16,6 +16,7 @@ from typing import Dict, Optional, Sequence, Tuple
 import torch
 
 from . import _native as N
+from .observability import nvtx_range
 
 _ERR_WORDS: Dict[int, torch.Tensor] = {}
 
@@ -167,7 +168,7 @@ def build_block_mask(total_frames: int, num_patches: int, window_size: int, n_fi
             counters=torch.zeros(4, dtype=torch.int32, **kw),
         )
     bufs_c = N.LvsaMaskBuffers(*[t[n].data_ptr() for n, _ in N.LvsaMaskBuffers._fields_])
-    with torch.cuda.device(device):
+    with torch.cuda.device(device), nvtx_range("lvsa_build_mask"):
         st = N.load().lvsa_build_mask(ctypes.byref(pat), ctypes.byref(bufs_c), _stream_ptr(device))
     N.check(st, "lvsa_build_mask")
     return BlockMask(
@@ -301,7 +302,7 @@ def block_sparse_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, ma
         getattr(mask, "token_offset", 0),
         int(q_tiles[0]) if q_tiles is not None else getattr(mask, "first_q_tile", 0),
         int(q_tiles[1]) if q_tiles is not None else 0, int(wait_timeout_us), int(inject_fault))
-    with torch.cuda.device(q.device):
+    with torch.cuda.device(q.device), nvtx_range("lvsa_attn_fwd_fp8" if fp8 else "lvsa_attn_fwd"):
         if fp8:
             st = N.load().lvsa_attn_fwd_fp8(ctypes.byref(args), ctypes.byref(sc_c), _stream_ptr(q.device))
         else:

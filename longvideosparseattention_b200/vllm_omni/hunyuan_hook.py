@@ -18,6 +18,7 @@ import torch
 from ..block_sparse import block_sparse_attention
 from ..sparse_attention import LVSAMetadata, compute_auto_kfi, compute_global_indices, \
     print_attention_mask_compact
+from ..observability import StepLogger
 from ..step_mask import SHARED
 from ._fallback import warn_fallback
 from .config import LVSAConfig
@@ -93,6 +94,7 @@ class HunyuanLVSAState:
         self._generation_seq_len: Optional[int] = None
         self._mask_log_last_step = -1
         self._engaged_logged = False
+        self._logger = StepLogger()
 
     def tick(self, layer_id: int, seq_len: int) -> int:
         if self._generation_seq_len is not None and seq_len != self._generation_seq_len:
@@ -110,7 +112,10 @@ class HunyuanLVSAState:
             else:
                 self._seen_ids.add(layer_id)
         if self._n_blocks is not None:
-            self._step = max(self._step, (self._call_count - 1) // (self._n_blocks * self._cfg_passes))
+            new = max(self._step, (self._call_count - 1) // (self._n_blocks * self._cfg_passes))
+            if new > self._step:
+                self._logger.step_boundary(new)   # LVSA_MEM_LOG / LVSA_STEP_TIME_LOG
+            self._step = new
         return self._step
 
     def key_frame_interval(self, total_latent_frames: int) -> Optional[int]:

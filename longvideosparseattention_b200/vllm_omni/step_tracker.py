@@ -10,7 +10,10 @@ call per transformer block)."""
 import threading
 from typing import Optional
 
+from ..observability import StepLogger
+
 _state = threading.local()
+_logger = StepLogger()
 _global_tracker: Optional["BlockCountStepTracker"] = None
 
 
@@ -76,6 +79,7 @@ class BlockCountStepTracker:
         if self._calibrated and self._n_blocks is not None and self._call_count >= self._n_blocks:
             self._call_count = 0
             self._step += 1
+            _logger.step_boundary(self._step)   # LVSA_MEM_LOG / LVSA_STEP_TIME_LOG
         _state.step = step
         return step
 
@@ -85,6 +89,7 @@ class BlockCountStepTracker:
             self._calibrated = True
             self._call_count = 0
             self._step = 1
+            _logger.step_boundary(1)
 
     @property
     def current_step(self) -> int:

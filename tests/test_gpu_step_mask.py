@@ -86,3 +86,13 @@ def test_device_step_equals_host_offset(graph):
         for a, b in zip(m.host_csr(), want.host_csr()):
             assert torch.equal(a, b), step
         assert torch.equal(m.window_bounds, want.window_bounds)
+
+
+def test_lvsa_stats_counts_the_launch():
+    from longvideosparseattention_b200 import build_block_mask, lvsa_stats
+    m = build_block_mask(21, 150, 2, 1, 4, 1, True, 30, device="cuda")
+    st = lvsa_stats(m, heads=3, head_dim=128)
+    ip, idx, _ = m.host_csr()
+    assert st["tiles"] == len(idx) == int(ip[-1])
+    assert st["dense_tiles"] == m.n_q_tiles * m.n_k_tiles and 0 < st["density"] <= 1
+    assert st["tile_flops"] == 4 * 128 * 128 * 128 * len(idx) * 3
