@@ -145,6 +145,12 @@ typedef struct LvsaAttnArgs {
   /* Test hook (0 in normal use): 1 makes CTA (0, 0, 0) skip its query-tile
    * load, so its waits expire and the path above runs. */
   int32_t inject_fault;
+  /* Video KEY tokens in k / v when they differ from the query tokens (ABI
+   * 102); <= 0: n_video.  A block-sparse layout whose key blocks are frames
+   * of another sequence (the reference's compact FlashInfer K/V): key token
+   * j belongs to frame (token_offset + j) / num_patches of frame_bits'
+   * column space, n_k_video_tiles = ceil(n_kv_video / block_k). */
+  int32_t n_kv_video;
 } LvsaAttnArgs;
 
 /* Block-sparse attention forward on tcgen05/TMEM, K/V read in place.

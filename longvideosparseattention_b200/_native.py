@@ -70,7 +70,8 @@ class LvsaAttnArgs(ctypes.Structure):
                 ("n_q_tiles", _i32), ("n_k_video_tiles", _i32),
                 ("frame_bits", _vp), ("tile_indptr", _vp), ("tile_indices", _vp),
                 ("tile_flags", _vp), ("error_word", _vp), ("token_offset", _i32), ("first_q_tile", _i32),
-                ("end_q_tile", _i32), ("wait_timeout_us", _i32), ("inject_fault", _i32)]
+                ("end_q_tile", _i32), ("wait_timeout_us", _i32), ("inject_fault", _i32),
+                ("n_kv_video", _i32)]
 
 
 LVSA_MAX_COPY_SEGMENTS = 64

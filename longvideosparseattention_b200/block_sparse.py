@@ -259,6 +259,9 @@ def block_sparse_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, ma
     if (mask.block_q, mask.block_k) != (ATTN_BLOCK_Q, ATTN_BLOCK_K):
         raise ValueError(f"the attention kernel needs a {ATTN_BLOCK_Q}x{ATTN_BLOCK_K} tile CSR, "
                          f"got {mask.block_q}x{mask.block_k}")
+    n_kv = int(k.shape[1])
+    if n_kv != Nv and n_kv != getattr(mask, "n_kv_video", Nv):
+        raise AssertionError(f"key length {n_kv} does not match the mask ({getattr(mask, 'n_kv_video', Nv)})")
     if Nv != mask.n_video or Nt != mask.n_text:
         raise AssertionError(f"sequence ({Nv} video, {Nt} text) does not match the mask "
                              f"({mask.n_video} video, {mask.n_text} text)")
@@ -301,7 +304,8 @@ def block_sparse_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, ma
         mask.tile_flags.data_ptr(), error_word(q.device).data_ptr(),
         getattr(mask, "token_offset", 0),
         int(q_tiles[0]) if q_tiles is not None else getattr(mask, "first_q_tile", 0),
-        int(q_tiles[1]) if q_tiles is not None else 0, int(wait_timeout_us), int(inject_fault))
+        int(q_tiles[1]) if q_tiles is not None else 0, int(wait_timeout_us), int(inject_fault),
+        n_kv if n_kv != Nv else 0)
     with torch.cuda.device(q.device), nvtx_range("lvsa_attn_fwd_fp8" if fp8 else "lvsa_attn_fwd"):
         if fp8:
             st = N.load().lvsa_attn_fwd_fp8(ctypes.byref(args), ctypes.byref(sc_c), _stream_ptr(q.device))

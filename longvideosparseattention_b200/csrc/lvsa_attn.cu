@@ -76,7 +76,7 @@ struct AttnParams {
   float* lse;
   float* text_lse;
   int64_t o_sb, o_st, o_sh, to_sb, to_st, to_sh;
-  int n_video, n_text, heads, kv_heads, T, P, words, nqv, nkv;
+  int n_video, n_kv, n_text, heads, kv_heads, T, P, words, nqv, nkv;  // n_kv: video keys
   float scale_log2;
   const uint32_t* frame_bits;
   const int32_t* indptr;
@@ -146,10 +146,10 @@ __device__ __forceinline__ void tile_mask(uint32_t (&am)[4], const AttnParams& p
   if (kt >= prm.nkv) {
     set_cols(am, 0, min(kBN, prm.n_text - (kt - prm.nkv) * kBN));
   } else if (text_row) {
-    set_cols(am, 0, min(kBN, prm.n_video - kt * kBN));
+    set_cols(am, 0, min(kBN, prm.n_kv - kt * kBN));
   } else {
     // Key tokens are numbered from the shard start; frames from the grid start.
-    const int ks = kt * kBN, kend = min(ks + kBN, prm.n_video);
+    const int ks = kt * kBN, kend = min(ks + kBN, prm.n_kv);
     int f = (prm.tok_off + ks) / prm.P, c0 = 0;
     while (ks + c0 < kend) {
       const int ce = min((f + 1) * prm.P - prm.tok_off, kend) - ks;
@@ -1021,8 +1021,9 @@ int launch(const LvsaAttnArgs* a, cudaStream_t stream, const LvsaFp8Scales* sc =
   int st;
   const int dt = kFp8 ? LVSA_DTYPE_E4M3 : (kBf16_ ? LVSA_DTYPE_BF16 : LVSA_DTYPE_F16);
   if ((st = make_map(&mq, a->q, a->batch, a->n_video, a->heads, D, dt))) return st;
-  if ((st = make_map(&mk, a->k, a->batch, a->n_video, a->kv_heads, D, dt))) return st;
-  if ((st = make_map(&mv, a->v, a->batch, a->n_video, a->kv_heads, D, dt))) return st;
+  const int n_kv = a->n_kv_video > 0 ? a->n_kv_video : a->n_video;
+  if ((st = make_map(&mk, a->k, a->batch, n_kv, a->kv_heads, D, dt))) return st;
+  if ((st = make_map(&mv, a->v, a->batch, n_kv, a->kv_heads, D, dt))) return st;
   const bool text_rows = a->n_text > 0 && a->text_q.ptr != nullptr;
   if (a->n_text > 0) {
     if ((st = make_map(&mtk, a->text_k, a->batch, a->n_text, a->kv_heads, D, dt))) return st;
@@ -1047,7 +1048,7 @@ int launch(const LvsaAttnArgs* a, cudaStream_t stream, const LvsaFp8Scales* sc =
   p.text_lse = text_rows ? a->text_lse : nullptr;
   p.o_sb = a->o.stride_b; p.o_st = a->o.stride_t; p.o_sh = a->o.stride_h;
   p.to_sb = a->text_o.stride_b; p.to_st = a->text_o.stride_t; p.to_sh = a->text_o.stride_h;
-  p.n_video = a->n_video; p.n_text = a->n_text; p.heads = a->heads; p.kv_heads = a->kv_heads;
+  p.n_video = a->n_video; p.n_kv = n_kv; p.n_text = a->n_text; p.heads = a->heads; p.kv_heads = a->kv_heads;
   p.T = a->total_frames; p.P = a->num_patches; p.words = a->frame_words;
   p.nqv = a->n_q_video_tiles; p.nkv = a->n_k_video_tiles;
   const float scale = a->scale > 0.f ? a->scale : 1.0f / std::sqrt(static_cast<float>(D));
@@ -1117,7 +1118,9 @@ int validate(const LvsaAttnArgs* a) {
   if (a->first_q_tile < 0 || a->first_q_tile > a->n_q_tiles) return LVSA_ERR_INVALID_ARG;
   if (a->end_q_tile > 0 && (a->end_q_tile < a->first_q_tile || a->end_q_tile > a->n_q_tiles))
     return LVSA_ERR_INVALID_ARG;
-  if (a->n_q_video_tiles != (a->n_video + kBlockQ - 1) / kBlockQ || a->n_k_video_tiles != (a->n_video + kBN - 1) / kBN ||
+  const long long n_kv = a->n_kv_video > 0 ? a->n_kv_video : a->n_video;
+  if (a->n_kv_video < 0 || a->token_offset + n_kv > grid_tokens) return LVSA_ERR_GEOMETRY;
+  if (a->n_q_video_tiles != (a->n_video + kBlockQ - 1) / kBlockQ || a->n_k_video_tiles != (n_kv + kBN - 1) / kBN ||
       a->frame_words != (a->total_frames + 31) / 32)
     return LVSA_ERR_GEOMETRY;
   if (a->n_text > 0 && (!a->text_k.ptr || !a->text_v.ptr)) return LVSA_ERR_INVALID_ARG;

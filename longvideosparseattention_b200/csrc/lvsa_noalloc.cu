@@ -94,7 +94,8 @@ extern "C" int lvsa_attn_fwd_fp8_noalloc(const LvsaAttnArgs* a, void* stream) {
   if (has_text && (!a->text_k.ptr || !a->text_v.ptr)) return LVSA_ERR_INVALID_ARG;
 
   const size_t B = a->batch, Nv = a->n_video, Nt = a->n_text, H = a->heads, Hk = a->kv_heads, D = a->head_dim;
-  const size_t tv = (Nv + 127) / 128, tt = (Nt + 127) / 128;
+  const size_t Nk = a->n_kv_video > 0 ? a->n_kv_video : Nv;  // video keys
+  const size_t tv = (Nv + 127) / 128, tk = (Nk + 127) / 128, tt = (Nt + 127) / 128;
   // Scratch layout: each part starts on a 256-byte boundary.
   size_t off = 0;
   auto take = [&off](size_t bytes) {
@@ -102,11 +103,11 @@ extern "C" int lvsa_attn_fwd_fp8_noalloc(const LvsaAttnArgs* a, void* stream) {
     off += round256(bytes);
     return at;
   };
-  const size_t o_q = take(B * Nv * H * D), o_k = take(B * Nv * Hk * D), o_v = take(B * Nv * Hk * D);
+  const size_t o_q = take(B * Nv * H * D), o_k = take(B * Nk * Hk * D), o_v = take(B * Nk * Hk * D);
   const size_t o_tq = text_rows ? take(B * Nt * H * D) : 0;
   const size_t o_tk = has_text ? take(B * Nt * Hk * D) : 0;
   const size_t o_tv = has_text ? take(B * Nt * Hk * D) : 0;
-  const size_t o_sq = take(B * H * tv * 4), o_sk = take(B * Hk * tv * 4), o_sv = take(B * Hk * tv * 4);
+  const size_t o_sq = take(B * H * tv * 4), o_sk = take(B * Hk * tk * 4), o_sv = take(B * Hk * tk * 4);
   const size_t o_stq = text_rows ? take(B * H * tt * 4) : 0;
   const size_t o_stk = has_text ? take(B * Hk * tt * 4) : 0;
   const size_t o_stv = has_text ? take(B * Hk * tt * 4) : 0;
@@ -123,8 +124,9 @@ extern "C" int lvsa_attn_fwd_fp8_noalloc(const LvsaAttnArgs* a, void* stream) {
 
   const int dt = a->dtype, b = a->batch, h = a->heads, hk = a->kv_heads, d = a->head_dim;
   if ((st = lvsa_quantize_e4m3(&a->q, dt, b, a->n_video, h, d, base + o_q, f32(o_sq), nullptr, stream))) return st;
-  if ((st = lvsa_quantize_e4m3(&a->k, dt, b, a->n_video, hk, d, base + o_k, f32(o_sk), nullptr, stream))) return st;
-  if ((st = lvsa_quantize_e4m3(&a->v, dt, b, a->n_video, hk, d, base + o_v, f32(o_sv), f32(o_ref), stream)))
+  const int nk = static_cast<int>(Nk);
+  if ((st = lvsa_quantize_e4m3(&a->k, dt, b, nk, hk, d, base + o_k, f32(o_sk), nullptr, stream))) return st;
+  if ((st = lvsa_quantize_e4m3(&a->v, dt, b, nk, hk, d, base + o_v, f32(o_sv), f32(o_ref), stream)))
     return st;
   if (has_text) {
     if ((st = lvsa_quantize_e4m3(&a->text_k, dt, b, a->n_text, hk, d, base + o_tk, f32(o_stk), nullptr, stream)))
@@ -149,8 +151,8 @@ extern "C" int lvsa_attn_fwd_fp8_noalloc(const LvsaAttnArgs* a, void* stream) {
     return t;
   };
   q8.q = view(o_q, Nv, H);
-  q8.k = view(o_k, Nv, Hk);
-  q8.v = view(o_v, Nv, Hk);
+  q8.k = view(o_k, Nk, Hk);
+  q8.v = view(o_v, Nk, Hk);
   if (has_text) {
     q8.text_k = view(o_tk, Nt, Hk);
     q8.text_v = view(o_tv, Nt, Hk);

@@ -456,11 +456,24 @@ def lvsa_sdpa(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor, k_glo
     return out
 
 
-def lvsa_flashinfer(query_padded, k_compact, v_compact, fi_wrapper, local_seq, fi_M):
-    """The reference's FlashInfer runner (lvsa/sparse_attention.py:709-742)
-    has no counterpart: every backend name routes to the sm_100a kernel via
-    ``sparse_windowed_attention``."""
-    raise NotImplementedError("use sparse_windowed_attention(...): one sm_100a kernel serves every backend")
+def lvsa_flashinfer(query_padded: torch.Tensor, k_compact: torch.Tensor, v_compact: torch.Tensor,
+                    fi_wrapper: Any, local_seq: int, fi_M: int) -> torch.Tensor:
+    """Drop-in for lvsa_flashinfer (lvsa/sparse_attention.py:709-742).
+
+    ``fi_wrapper`` is a planned ``bsr.LvsaBlockSparseWrapper`` (same plan
+    arguments as the reference's flashinfer.BlockSparseAttentionWrapper:
+    the frame CSR fi_indptr / fi_indices, M = fi_M, N = compact_n x P,
+    R = C = P) or any object with that ``run(q, k, v)``.
+    query_padded [B, M, H, D], k_compact / v_compact [B, compact_N, Hkv, D];
+    returns [B, local_seq, H, D]."""
+    from .bsr import LvsaBlockSparseWrapper
+    if isinstance(fi_wrapper, LvsaBlockSparseWrapper):
+        out = fi_wrapper.run(query_padded, k_compact, v_compact)       # one launch for the batch
+    else:
+        out = query_padded.new_empty(query_padded.shape[0], fi_M, *query_padded.shape[2:])
+        for b in range(query_padded.shape[0]):
+            out[b] = fi_wrapper.run(query_padded[b], k_compact[b], v_compact[b])
+    return out[:, :local_seq]
 
 
 def sparse_windowed_attention(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor,
