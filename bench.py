@@ -674,6 +674,53 @@ def run_prologue(args, cfg):
         "clocks": clocks, "gpu_launches": 2 * args.steps}), flush=True)
 
 
+def run_out_proj(args, cfg):
+    """--out-proj: the to_out projection of the configuration's attention
+    output (tokens x H*D -> H*D, Wan / HunyuanVideo / CogVideoX model dim)
+    on the tcgen05 GEMM (lvsa_out_proj), against torch's Linear (cuBLAS) on
+    the same operands.  Inputs larger than L2 (the attention output)."""
+    import torch
+    import torch.nn.functional as F
+    from longvideosparseattention_b200.out_proj import out_projection
+    dev = torch.device("cuda", 0)
+    S, H, D = cfg["T"] * cfg["P"], cfg["H"], cfg["D"]
+    K = Nout = H * D
+    g = torch.Generator(device=dev).manual_seed(3)
+    o = torch.randn(1, S, H, D, device=dev, generator=g).bfloat16()
+    w = (torch.randn(Nout, K, device=dev, generator=g) / K ** 0.5).bfloat16()
+    b = torch.randn(Nout, device=dev, generator=g).bfloat16()
+    y = torch.empty(S, Nout, device=dev, dtype=torch.bfloat16)
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / args.steps
+
+    with ClockSampler(0) as clk:
+        ms = timed(lambda: out_projection(o, w, b, out=y))
+    ms_torch = timed(lambda: F.linear(o.view(S, K), w, b))
+    flop = 2.0 * S * K * Nout
+    pk, src = peaks()
+    tf = flop / (ms * 1e-3) / 1e12
+    print(json.dumps({
+        "metric": "to_out projection TFLOP/s", "value": round(tf, 1), "unit": "TFLOP/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"{args.config} to_out", "m": S, "k": K, "n": Nout, "bias": True},
+        "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": pk.get("bf16_tflops"), "unit": "TFLOP/s",
+                     "frac": round(tf / pk.get("bf16_tflops"), 4), "traffic": None,
+                     "peak_source": f"{src} bf16_tflops (burst: a short kernel timed alone)"},
+        "torch_linear_ms": round(ms_torch, 4), "torch_linear_tflops": round(flop / (ms_torch * 1e-3) / 1e12, 1),
+        "clocks": clk.summary(), "gpu_launches": args.steps}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -692,6 +739,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
     ap.add_argument("--no-peak", action="store_true", help="--fp8: skip the in-run E4M3 GEMM peak measurement")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--out-proj", action="store_true",
+                    help="time the to_out projection GEMM (tcgen05) against torch's Linear")
     ap.add_argument("--prologue", action="store_true",
                     help="time the fused QK prologue (norm + RoPE) instead of the attention step")
     args = ap.parse_args()
@@ -703,6 +752,8 @@ def main():
         args.cpu_baseline = False
     if args.prologue:
         run_prologue(args, cfg)
+    elif args.out_proj:
+        run_out_proj(args, cfg)
     elif args.impl == "reference":
         run_reference(args, cfg)
     else:

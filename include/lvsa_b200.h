@@ -264,6 +264,25 @@ int lvsa_qk_prologue(const LvsaQkPrologue* args, void* stream);
 #define LVSA_NOALLOC_SCRATCH_BYTES (96u * 1024u * 1024u)
 int lvsa_attn_fwd_fp8_noalloc(const LvsaAttnArgs* args, void* stream);
 
+/* ---- output projection (the to_out Linear after attention) ----------
+ * out[m, n] = sum_k a[m, k] * weight[n, k] (+ bias[n]) on tcgen05 / TMEM,
+ * bf16 or f16 in and out, fp32 accumulation.  `a` is the attention output
+ * read in place: an [B, S, H, D] token-major o is [m = B*S, k = H*D] with
+ * lda = H*D (or its token stride); `weight` is an nn.Linear weight
+ * [out_features, in_features].  Replaces attn.to_out[0] after the LVSA
+ * attention (lvsa/adapters/wan.py:121-131, lvsa/adapters/hunyuan_video.py:
+ * 207-217).  k must be a multiple of 64, n of 32; rows 16-byte aligned. */
+typedef struct LvsaOutProjArgs {
+  const void* a;       /* [m, k], row stride lda elements                      */
+  const void* weight;  /* [n, k], row stride ldw elements                      */
+  const void* bias;    /* [n] or NULL                                          */
+  void* out;           /* [m, n], row stride ldo elements                      */
+  int64_t lda, ldw, ldo;
+  int32_t m, n, k, dtype;
+  int32_t* error_word; /* optional device int: LVSA_ERR_DEVICE_TIMEOUT          */
+} LvsaOutProjArgs;
+int lvsa_out_proj(const LvsaOutProjArgs* args, void* stream);
+
 /* ---- batched strided row copies (gather / scatter of an exchange) ----
  * No counterpart in the reference (its only multi-GPU exchange is one
  * all_reduce).  Packs and unpacks the Ulysses all-to-all buffers in one

@@ -27,7 +27,7 @@ LVSA_DTYPE_F16 = 1
 LVSA_MAX_FRAMES = 2048
 
 EXPORTED_SYMBOLS = ("lvsa_mask_layout", "lvsa_build_mask", "lvsa_attn_fwd", "lvsa_quantize_e4m3",
-                    "lvsa_attn_fwd_fp8", "lvsa_attn_fwd_fp8_noalloc", "lvsa_qk_prologue", "lvsa_copy_segments", "lvsa_status_str",
+                    "lvsa_attn_fwd_fp8", "lvsa_attn_fwd_fp8_noalloc", "lvsa_qk_prologue", "lvsa_copy_segments", "lvsa_out_proj", "lvsa_status_str",
                     "lvsa_abi_version")
 LVSA_DTYPE_E4M3 = 2
 LVSA_DTYPE_F32 = 3
@@ -83,6 +83,11 @@ class LvsaCopySegment(ctypes.Structure):
                 ("heads", _i32)]
 
 
+class LvsaOutProjArgs(ctypes.Structure):
+    _fields_ = [("a", _vp), ("weight", _vp), ("bias", _vp), ("out", _vp), ("lda", _i64), ("ldw", _i64),
+                ("ldo", _i64), ("m", _i32), ("n", _i32), ("k", _i32), ("dtype", _i32), ("error_word", _vp)]
+
+
 class LvsaQkPrologue(ctypes.Structure):
     _fields_ = [("x", LvsaTensor), ("dtype", _i32), ("batch", _i32), ("seq", _i32), ("heads", _i32),
                 ("head_dim", _i32), ("norm", _i32), ("weight_dtype", _i32), ("weight", _vp), ("bias", _vp),
@@ -131,6 +136,8 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
         lib.lvsa_attn_fwd_fp8_noalloc.restype = ctypes.c_int
         lib.lvsa_qk_prologue.argtypes = [ctypes.POINTER(LvsaQkPrologue), _vp]
         lib.lvsa_qk_prologue.restype = ctypes.c_int
+        lib.lvsa_out_proj.argtypes = [ctypes.POINTER(LvsaOutProjArgs), _vp]
+        lib.lvsa_out_proj.restype = ctypes.c_int
         lib.lvsa_copy_segments.argtypes = [ctypes.POINTER(LvsaCopySegment), _i32, _i32, _vp]
         lib.lvsa_copy_segments.restype = ctypes.c_int
         lib.lvsa_status_str.argtypes = [ctypes.c_int]
