@@ -6,13 +6,15 @@
 // B operand.  Replaces the model's `attn.to_out[0]` Linear after attention
 // (lvsa/adapters/wan.py:121-131, lvsa/adapters/hunyuan_video.py:207-217).
 //
-// One CTA per 128 x 256 output tile (grid: N tiles fastest, so the CTAs that
-// share a tile of A run together and read it from L2).  Warp 0 streams A and
+// Persistent: one CTA per SM walks 128 x 256 output tiles (N tiles fastest,
+// so the CTAs on one row block of A read it from L2).  Warp 0 streams A and
 // W tiles of 64 K-columns through a 4-stage TMA ring (128B swizzle, no
-// multicast); warp 1 allocates 256 TMEM columns and issues the MMAs
-// (128 x 256 x 16 per instruction) from one thread; warps 2-5 read the
-// accumulator back (one row per thread), add the bias and store.  Every
-// wait is bounded (error word, drain, free TMEM, return).
+// multicast) across tile boundaries; warp 1 allocates two 256-column TMEM
+// accumulators and issues the MMAs (128 x 256 x 16 per instruction) from
+// one thread, alternating accumulators per tile; warps 2-5 read a finished
+// accumulator back (one row per thread), add the bias and store while the
+// MMAs of the next tile run into the other one.  Every wait is bounded
+// (error word, drain, free TMEM, return).
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -60,72 +62,93 @@ __global__ void __launch_bounds__(kGThreads, 1)
   uint8_t* sA = smem;
   uint8_t* sB = smem + kGStages * kATile;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kGStages * (kATile + kBTile));
-  uint64_t* full = bars;                 // [stages]
-  uint64_t* empty = bars + kGStages;     // [stages]
-  uint64_t* acc_full = bars + 2 * kGStages;
-  uint64_t* drain = acc_full + 1;
+  uint64_t* full = bars;                  // [stages] A and W tiles landed
+  uint64_t* empty = bars + kGStages;      // [stages] their MMAs retired
+  uint64_t* acc_full = bars + 2 * kGStages;  // [2] accumulator b holds a finished tile
+  uint64_t* acc_empty = acc_full + 2;        // [2] epilogue has read accumulator b
+  uint64_t* drain = acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* never = reinterpret_cast<volatile int*>(tmem_slot + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * kGN, m0 = blockIdx.y * kGM;
   const int kblocks = prm.K / kGK;
+  const int n_tiles_n = (prm.N + kGN - 1) / kGN;
+  const int n_tiles = n_tiles_n * ((prm.M + kGM - 1) / kGM);
+  // Persistent: CTA c takes tiles c, c + grid, ...; N tiles fastest, so the
+  // CTAs working on one row block of A at a time read it from L2.
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kGStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(acc_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 128);
+    }
     mbar_init(drain, 1);
     *abort = 0;
     *never = 0;
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, kGN);
+    tmem_alloc(tmem_slot, 2 * kGN);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tacc = *tmem_slot;
+  const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
     if (lane == 0) {
       tma_prefetch_desc(&tm_a);
       tma_prefetch_desc(&tm_w);
-      int issued = 0;
-      for (int kb = 0; kb < kblocks; ++kb) {
-        const int s = kb % kGStages;
-        if (kb >= kGStages && !mbar_wait(&empty[s], ((kb / kGStages) - 1) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT))
-          break;
-        mbar_expect_tx(&full[s], kATile + kBTile);
-        tma_load_2d(sA + s * kATile, &tm_a, &full[s], kb * kGK, m0);
-        tma_load_2d(sB + s * kBTile, &tm_w, &full[s], kb * kGK, n0);
-        issued = kb + 1;
+      int g = 0;  // global load counter across tiles
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < n_tiles; t += gridDim.x) {
+        const int n0 = (t % n_tiles_n) * kGN, m0 = (t / n_tiles_n) * kGM;
+        for (int kb = 0; kb < kblocks; ++kb, ++g) {
+          const int s = g % kGStages;
+          if (g >= kGStages &&
+              !(ok = mbar_wait(&empty[s], ((g / kGStages) - 1) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT)))
+            break;
+          mbar_expect_tx(&full[s], kATile + kBTile);
+          tma_load_2d(sA + s * kATile, &tm_a, &full[s], kb * kGK, m0);
+          tma_load_2d(sB + s * kBTile, &tm_w, &full[s], kb * kGK, n0);
+        }
       }
       if (*abort)  // drain our own copies before the CTA retires
-        for (int kb = issued > kGStages ? issued - kGStages : 0; kb < issued; ++kb)
-          mbar_wait(&full[kb % kGStages], (kb / kGStages) & 1, never, nullptr, 0);
+        for (int x = g > kGStages ? g - kGStages : 0; x < g; ++x)
+          mbar_wait(&full[x % kGStages], (x / kGStages) & 1, never, nullptr, 0);
     }
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_f16(kGM, kGN, kBf16, false);
       const uint32_t a_base = smem_u32(sA), b_base = smem_u32(sB);
       bool ok = true;
-      for (int kb = 0; ok && kb < kblocks; ++kb) {
-        const int s = kb % kGStages;
-        if (!(ok = mbar_wait(&full[s], (kb / kGStages) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT))) break;
+      int g = 0, it = 0;
+      for (int t = blockIdx.x; ok && t < n_tiles; t += gridDim.x, ++it) {
+        const int buf = it & 1;
+        const uint32_t tacc = tmem + buf * kGN;
+        // Accumulator `buf` was last used by tile it - 2: wait for its epilogue.
+        if (it >= 2 && !(ok = mbar_wait(&acc_empty[buf], ((it >> 1) - 1) & 1, abort, prm.err,
+                                        LVSA_ERR_DEVICE_TIMEOUT)))
+          break;
         tc_fence_after();
+        for (int kb = 0; kb < kblocks; ++kb, ++g) {
+          const int s = g % kGStages;
+          if (!(ok = mbar_wait(&full[s], (g / kGStages) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT))) break;
+          tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < kGK / 16; ++kk)  // 32 bytes of K per instruction
-          mma_ss(tacc, sdesc_sw128(a_base + s * kATile + kk * 32, 16, 1024),
-                 sdesc_sw128(b_base + s * kBTile + kk * 32, 16, 1024), idesc, (kb | kk) > 0);
-        mma_commit(&empty[s]);
+          for (int kk = 0; kk < kGK / 16; ++kk)  // 32 bytes of K per instruction
+            mma_ss(tacc, sdesc_sw128(a_base + s * kATile + kk * 32, 16, 1024),
+                   sdesc_sw128(b_base + s * kBTile + kk * 32, 16, 1024), idesc, (kb | kk) > 0);
+          mma_commit(&empty[s]);
+        }
+        if (ok) mma_commit(&acc_full[buf]);
       }
-      if (ok) mma_commit(acc_full);
       mma_commit(drain);
       mbar_wait(drain, 0, never, nullptr, 0);
     }
@@ -133,21 +156,28 @@ __global__ void __launch_bounds__(kGThreads, 1)
     // warps 2..5: TMEM lanes 32 * (warp % 4) .. + 31, one output row each
     using Elem = typename std::conditional<kBf16, __nv_bfloat16, __half>::type;
     const int q = warp & 3;
-    const int row = m0 + q * 32 + lane;
-    if (__all_sync(0xFFFFFFFFu, mbar_wait(acc_full, 0, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT))) {
+    const Elem* bias = static_cast<const Elem*>(prm.bias);
+    int it = 0;
+    for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++it) {
+      const int buf = it & 1;
+      const int n0 = (t % n_tiles_n) * kGN, m0 = (t / n_tiles_n) * kGM;
+      if (!__all_sync(0xFFFFFFFFu, mbar_wait(&acc_full[buf], (it >> 1) & 1, abort, prm.err,
+                                             LVSA_ERR_DEVICE_TIMEOUT)))
+        break;
       tc_fence_after();
-      const Elem* bias = static_cast<const Elem*>(prm.bias);
+      const uint32_t tacc = tmem + buf * kGN + (static_cast<uint32_t>(q * 32) << 16);
+      const int row = m0 + q * 32 + lane;
       Elem* orow = static_cast<Elem*>(prm.out) + static_cast<int64_t>(row) * prm.ldo + n0;
 #pragma unroll 1
       for (int c = 0; c < kGN / 32; ++c) {
-        uint32_t t[32];
-        tmem_ld32(tacc + (static_cast<uint32_t>(q * 32) << 16) + c * 32, t);
+        uint32_t t32[32];
+        tmem_ld32(tacc + c * 32, t32);
         const int col = n0 + c * 32;
         if (row < prm.M && col < prm.N) {
           uint32_t pk[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            float x0 = __uint_as_float(t[2 * i]), x1 = __uint_as_float(t[2 * i + 1]);
+            float x0 = __uint_as_float(t32[2 * i]), x1 = __uint_as_float(t32[2 * i + 1]);
             if (bias) {
               x0 += static_cast<float>(bias[col + 2 * i]);
               x1 += static_cast<float>(bias[col + 2 * i + 1]);
@@ -165,6 +195,9 @@ __global__ void __launch_bounds__(kGThreads, 1)
           for (int i = 0; i < 4; ++i) dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
         }
       }
+      // The accumulator's columns are read: the next tile's MMAs may reuse it.
+      tc_fence_before();
+      mbar_arrive(&acc_empty[buf]);
     }
   }
 
@@ -172,7 +205,7 @@ __global__ void __launch_bounds__(kGThreads, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tacc, kGN);
+    tmem_dealloc(tmem, 2 * kGN);
   }
 }
 
@@ -236,7 +269,10 @@ extern "C" int lvsa_out_proj(const LvsaOutProjArgs* a, void* stream) {
   auto kern = bf16 ? lvsa_out_proj_kernel<true> : lvsa_out_proj_kernel<false>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kGSmem) != cudaSuccess)
     return LVSA_ERR_CUDA;
-  dim3 grid((a->n + kGN - 1) / kGN, (a->m + kGM - 1) / kGM);
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const long long tiles = static_cast<long long>((a->n + kGN - 1) / kGN) * ((a->m + kGM - 1) / kGM);
+  dim3 grid(static_cast<unsigned>(tiles < sms ? tiles : sms));
   kern<<<grid, kGThreads, kGSmem, static_cast<cudaStream_t>(stream)>>>(ma, mw, p);
   return cudaGetLastError() == cudaSuccess ? LVSA_OK : LVSA_ERR_CUDA;
 }
