@@ -65,6 +65,9 @@ constexpr int kMmaWarp = kSoftmaxWarps + 1;
 constexpr int kThreads = 32 * (kSoftmaxWarps + 2);
 constexpr uint32_t kTmemCols = 512;
 constexpr float kNegInf = -INFINITY;
+#ifndef LVSA_S3
+#define LVSA_S3 1
+#endif
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O only when the max grows by > 2^8
 
 struct AttnParams {
@@ -111,7 +114,7 @@ struct Smem {
   static constexpr int kK = kQ + kTile;
   static constexpr int kV = kK + SK * kTile;
   static constexpr int kBar = kV + SV * kTile;
-  static constexpr int kNumBars = 2 * SK + 2 * SV + 8;
+  static constexpr int kNumBars = 2 * SK + 2 * SV + 12;
   static constexpr int kMisc = kBar + kNumBars * 8;
   static constexpr int kBytes = kMisc + 16 + 1024;  // + alignment slack
   static_assert(kBytes <= 232448, "shared memory");
@@ -278,6 +281,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                      const __grid_constant__ CUtensorMap tm_tk, const __grid_constant__ CUtensorMap tm_tv,
                      const AttnParams prm) {
   using L = Smem<D, SK, SV, kFp8>;
+  // S/P buffers in TMEM: two (the classes alternate buffers, so S(j+2) waits
+  // for PV(j)); three when the O buffers are narrow enough to leave room
+  // (D = 64: 3 x 128 + 2 x 64 = 512 columns), so S(j+3) follows PV(j) and a
+  // class's next S is issued while the other class still runs its softmax.
+  constexpr int kNB = (D == 64 && LVSA_S3) ? 3 : 2;
+  constexpr int kOStride = kNB == 3 ? D : 128;
+  static_assert(kNB * 128 + 2 * kOStride <= static_cast<int>(kTmemCols), "TMEM columns");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem + L::kQ;
@@ -289,9 +299,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* v_full = k_full + SK;       // [SV]
   uint64_t* k_empty = v_full + SV;       // [SK] K stage free: the S of its tile is done
   uint64_t* v_empty = k_empty + SK;      // [SV] V stage free: the PV of its tile is done
-  uint64_t* s_full = v_empty + SV;       // [2] S buffer c holds S(j), j % 2 == c
-  uint64_t* p_full = s_full + 2;         // [2] P(j) written into buffer c
-  uint64_t* o_done = p_full + 2;         // every MMA of the CTA retired
+  uint64_t* s_full = v_empty + SV;       // [kNB] S buffer b holds S(j), j % kNB == b
+  uint64_t* p_full = s_full + 3;         // [kNB] P(j) written into buffer b
+  uint64_t* pv_done = p_full + 3;        // [2] (kNB == 3) PV of class c retired
+  uint64_t* o_done = pv_done + 2;        // every MMA of the CTA retired
   uint64_t* drain = o_done + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMisc);
   volatile int* abort = reinterpret_cast<volatile int*>(smem + L::kMisc + 4);
@@ -315,10 +326,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&v_full[s], 1);
       mbar_init(&v_empty[s], 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kNB; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 128);
     }
+    for (int i = 0; i < 2; ++i) mbar_init(&pv_done[i], 1);
     mbar_init(o_done, 1);
     mbar_init(drain, 1);
     *abort = 0;
@@ -333,7 +345,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tS = tmem, tO = tmem + 256;
+  // TMEM: kNB S/P buffers of 128 columns, then the two classes' O buffers.
+  const uint32_t tS = tmem, tO = tmem + kNB * 128;
 
   if (warp == kProducerWarp) {
     // ---------------------------------------------------------- producer
@@ -390,13 +403,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t idO = idesc_f16(kBM, D, kFmt1, true);
       const uint32_t q_base = smem_u32(sQ), k_base = smem_u32(sK), v_base = smem_u32(sV);
       auto issue_s = [&](int jj) {
-        const uint32_t kb = k_base + (jj % SK) * L::kTile, dS = tS + (jj & 1) * 128;
+        const uint32_t kb = k_base + (jj % SK) * L::kTile, dS = tS + (jj % kNB) * 128;
 #pragma unroll
         for (int kk = 0; kk < D * L::kElem / 32; ++kk) {  // 32 bytes of Q and K per instruction
           const uint32_t off = (kk >> 2) * kChunk + (kk & 3) * 32;
           mma_ss_any<kFp8>(dS, sdesc_sw128(q_base + off, 16, 1024), sdesc_sw128(kb + off, 16, 1024), idS, kk > 0);
         }
-        mma_commit(&s_full[jj & 1]);
+        mma_commit(&s_full[jj % kNB]);
         mma_commit(&k_empty[jj % SK]);
       };
       bool ok = mbar_wait(q_full, 0, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT, prm.wait_ns) &&
@@ -405,29 +418,33 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         issue_s(0);
       }
-      if (ok && n > 1 && (ok = mbar_wait(&k_full[1 % SK], (1 / SK) & 1, abort, prm.err,
-                                         LVSA_ERR_DEVICE_TIMEOUT, prm.wait_ns))) {
-        tc_fence_after();
-        issue_s(1);
-      }
+      for (int jj = 1; ok && jj < kNB && jj < n; ++jj)
+        if ((ok = mbar_wait(&k_full[jj % SK], (jj / SK) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT,
+                            prm.wait_ns))) {
+          tc_fence_after();
+          issue_s(jj);
+        }
       for (int j = 0; ok && j < n; ++j) {
         const int c = j & 1, it = j >> 1;
-        if (!(ok = mbar_wait(&p_full[c], it & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT, prm.wait_ns))) break;
+        if (!(ok = mbar_wait(&p_full[j % kNB], (j / kNB) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT,
+                             prm.wait_ns)))
+          break;
         if (!(ok = mbar_wait(&v_full[j % SV], (j / SV) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT, prm.wait_ns))) break;
         tc_fence_after();
-        const uint32_t vb = v_base + (j % SV) * L::kTile, pa = tS + c * 128, dO = tO + c * 128;
+        const uint32_t vb = v_base + (j % SV) * L::kTile, pa = tS + (j % kNB) * 128, dO = tO + c * kOStride;
 #pragma unroll
         for (int kk = 0; kk < kBN * L::kElem / 32; ++kk)  // 32 / kElem keys per instruction
           mma_ts_any<kFp8>(dO, pa + kk * 8, sdesc_sw128(vb + kk * (32 / L::kElem) * 128, kChunk, 1024), idO,
                            (it > 0 || kk > 0));
         mma_commit(&v_empty[j % SV]);
-        if (j + 2 < n) {
-          // S buffer c: P(j) was read by PV(j), issued just before.
-          if (!(ok = mbar_wait(&k_full[(j + 2) % SK], ((j + 2) / SK) & 1, abort, prm.err,
+        if constexpr (kNB == 3) mma_commit(&pv_done[c]);
+        if (j + kNB < n) {
+          // S buffer j % kNB: P(j) was read by PV(j), issued just before.
+          if (!(ok = mbar_wait(&k_full[(j + kNB) % SK], ((j + kNB) / SK) & 1, abort, prm.err,
                                LVSA_ERR_DEVICE_TIMEOUT, prm.wait_ns)))
             break;
           tc_fence_after();
-          issue_s(j + 2);
+          issue_s(j + kNB);
         }
       }
       if (ok) mma_commit(o_done);
@@ -446,7 +463,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int fq = text_row ? 0 : min((prm.tok_off + tok) / prm.P, prm.T - 1);
     const uint32_t* fbits = prm.frame_bits + static_cast<size_t>(fq) * prm.words;
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    const uint32_t tSc = tS + cls * 128 + lane_base;  // my S / P buffer
     const float sl2_base = prm.scale_log2;
     float sq = 1.f, vref = 1.f;
     if constexpr (kFp8) {
@@ -476,7 +492,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       uint32_t am[4] = {~0u, ~0u, ~0u, ~0u};
       if (flag) tile_mask(am, prm, kt, text_row, fbits);
-      if (!__all_sync(0xFFFFFFFFu, mbar_wait(&s_full[cls], it & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT, prm.wait_ns))) {
+      const uint32_t tSc = tS + (j % kNB) * 128 + lane_base;  // this tile's S / P buffer
+      if (!__all_sync(0xFFFFFFFFu, mbar_wait(&s_full[j % kNB], (j / kNB) & 1, abort, prm.err,
+                                             LVSA_ERR_DEVICE_TIMEOUT, prm.wait_ns))) {
         ok = false;
         break;
       }
@@ -494,13 +512,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (it == 0) {
         m = m_new;  // my O buffer has not been written yet
       } else {
-        // Lazy rescale of my O buffer.  It last received PV(j-2), which was
-        // issued before S(j): the s_full commit above covers it.
+        // Lazy rescale of my O buffer.  It last received PV(j-2).  With two
+        // S buffers that was issued before S(j), so the s_full commit above
+        // covers it; with three, S(j) follows PV(j-3): wait for PV(j-2).
         const bool need = m_new > m + kRescaleThreshold;
         if (__any_sync(0xFFFFFFFFu, need)) {
+          if constexpr (kNB == 3) {
+            if (!__all_sync(0xFFFFFFFFu, mbar_wait(&pv_done[cls], (it - 1) & 1, abort, prm.err,
+                                                   LVSA_ERR_DEVICE_TIMEOUT, prm.wait_ns))) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+          }
           const float alpha = need ? ex2_approx(m - m_new) : 1.f;
           if (need) m = m_new;
-          const uint32_t tOc = tO + cls * 128 + lane_base;
+          const uint32_t tOc = tO + cls * kOStride + lane_base;
 #pragma unroll
           for (int c = 0; c < D / 32; ++c) {
             uint32_t t[32];
@@ -523,7 +550,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       store_p<kFp8>(tSc + kPHalf, pk);
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&p_full[cls]);
+      mbar_arrive(&p_full[j % kNB]);
     }
     // ---------------------------------------------------------- epilogue
     // Merge the two classes: O = (a0 O0 + a1 O1) / (a0 l0 + a1 l1) with
@@ -565,7 +592,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t col = cls * (D / 2) + c * 32;
           uint32_t t0[32], t1[32];
           tmem_ld32(tO + lane_base + col, t0);
-          if (use1) tmem_ld32(tO + 128 + lane_base + col, t1);
+          if (use1) tmem_ld32(tO + kOStride + lane_base + col, t1);
           if (valid && obase) {
             uint32_t pk[16];
 #pragma unroll
