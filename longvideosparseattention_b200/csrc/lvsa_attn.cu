@@ -52,6 +52,17 @@
 #include "../../include/lvsa_b200.h"
 #include "lvsa_ptx.cuh"
 
+// Instrumentation build only (-DLVSA_PROFILE): clock64 totals per role of
+// the tile-pair kernel, read back by lvsa_prof_read.  Compiled out otherwise.
+#ifdef LVSA_PROFILE
+__device__ unsigned long long g_lvsa_prof[16];
+#define LVSA_CLK(x) const long long x = clock64()
+#define LVSA_PROF_ADD(i, v) atomicAdd(&g_lvsa_prof[i], static_cast<unsigned long long>(v))
+#else
+#define LVSA_CLK(x)
+#define LVSA_PROF_ADD(i, v)
+#endif
+
 namespace lvsa {
 namespace {
 
@@ -697,6 +708,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* never = reinterpret_cast<volatile int*>(smem + L::kMisc + 8);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  LVSA_CLK(t_cta0);
   const int h = blockIdx.y, b = blockIdx.z;
   // Pairs of video rows [row0, pair_ve), then pairs of text rows [pair_ts, pair_end).
   const int x = blockIdx.x;
@@ -806,7 +818,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int nc[2] = {n0, n1};
       // S_c(i) from load g; `last`: no later S reads that K stage.
       auto issue_s = [&](int c, int g, bool last) -> bool {
+        LVSA_CLK(t_k0);
         if (!mbar_wait(&k_full[g % SK], (g / SK) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT, prm.wait_ns)) return false;
+        LVSA_CLK(t_k1);
+        LVSA_PROF_ADD(4, t_k1 - t_k0);
         tc_fence_after();
         const uint32_t kb = k_base + (g % SK) * L::kTile, qb = q_base + c * L::kTile, dS = tS + c * 128;
 #pragma unroll
@@ -819,8 +834,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         return true;
       };
       auto issue_pv = [&](int c, int i, int g, bool last) -> bool {
+        LVSA_CLK(t_p0);
         if (!mbar_wait(&p_full[c], i & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT, prm.wait_ns)) return false;
+        LVSA_CLK(t_p1);
         if (!mbar_wait(&v_full[g % SV], (g / SV) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT, prm.wait_ns)) return false;
+        LVSA_CLK(t_p2);
+        LVSA_PROF_ADD(2, t_p1 - t_p0);
+        LVSA_PROF_ADD(3, t_p2 - t_p1);
         tc_fence_after();
         const uint32_t vb = v_base + (g % SV) * L::kTile, pa = tS + c * 128, dO = tO + c * 128;
 #pragma unroll
@@ -897,10 +917,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       uint32_t am[4] = {~0u, ~0u, ~0u, ~0u};
       if (flag) tile_mask(am, prm, kt, text_row, fbits);
+      LVSA_CLK(t_w0);
       if (!__all_sync(0xFFFFFFFFu, mbar_wait(&s_full[cls], it & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT, prm.wait_ns))) {
         ok = false;
         break;
       }
+      LVSA_CLK(t_w1);
+      if (lane == 0) LVSA_PROF_ADD(0, t_w1 - t_w0);
       tc_fence_after();
       uint32_t sv[64];
       float mx_hi;
@@ -943,6 +966,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&p_full[cls]);
+      LVSA_CLK(t_w2);
+      if (lane == 0) {
+        LVSA_PROF_ADD(1, t_w2 - t_w1);
+        LVSA_PROF_ADD(5, 1);
+      }
     }
     // ---------------------------------------------------------- epilogue
     using Elem = typename std::conditional<kBf16, __nv_bfloat16, __half>::type;
@@ -991,6 +1019,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
+  LVSA_CLK(t_cta1);
+  if (threadIdx.x == 0) {
+    LVSA_PROF_ADD(6, t_cta1 - t_cta0);
+    LVSA_PROF_ADD(7, 1);
+  }
   if (warp == kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
@@ -1256,3 +1289,12 @@ extern "C" const char* lvsa_status_str(int status) {
 }
 
 extern "C" int lvsa_abi_version(void) { return 102; }
+
+#ifdef LVSA_PROFILE
+// Instrumentation build only: copy out and clear the role totals.
+extern "C" int lvsa_prof_read(unsigned long long* out16) {
+  if (cudaMemcpyFromSymbol(out16, g_lvsa_prof, sizeof(g_lvsa_prof)) != cudaSuccess) return LVSA_ERR_CUDA;
+  unsigned long long z[16] = {};
+  return cudaMemcpyToSymbol(g_lvsa_prof, z, sizeof(z)) == cudaSuccess ? LVSA_OK : LVSA_ERR_CUDA;
+}
+#endif
