@@ -755,32 +755,19 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == kProducerWarp) {
     // ---------------------------------------------------------- producer
-    // Two independent streams: lane 0 the query tiles and the K ring, lane
-    // 1 the V ring.  Both walk the same load sequence; a K stage is freed by
-    // its S MMA, a V stage by its PV MMA, so neither ring waits on the other
-    // (one thread issuing K(g+1) only after V(g) held the K prefetch behind
-    // the shallow V ring).
-    if (lane < 2 && nmax > 0) {
-      const bool kside = lane == 0;
+    if (lane == 0 && nmax > 0) {
       const CUtensorMap* mq = text_row ? &tm_tq : &tm_q;
+      tma_prefetch_desc(mq);
+      tma_prefetch_desc(&tm_k);
+      tma_prefetch_desc(&tm_v);
       const bool skip_q = prm.inject && (blockIdx.x | blockIdx.y | blockIdx.z) == 0;
-      if (kside) {
-        tma_prefetch_desc(mq);
-        tma_prefetch_desc(&tm_k);
-        if (!skip_q) {
-          mbar_expect_tx(q_full, (has_b ? 2 : 1) * L::kTile);
-          for (int t = 0; t < (has_b ? 2 : 1); ++t)
+      if (!skip_q) {
+        mbar_expect_tx(q_full, (has_b ? 2 : 1) * L::kTile);
+        for (int t = 0; t < (has_b ? 2 : 1); ++t)
 #pragma unroll
-            for (int c = 0; c < L::kCh; ++c)
-              tma_load_4d(sQ + t * L::kTile + c * kChunk, mq, q_full, c * (128 / L::kElem), h, tok_a + t * kBM, b);
-        }
-      } else {
-        tma_prefetch_desc(&tm_v);
+          for (int c = 0; c < L::kCh; ++c)
+            tma_load_4d(sQ + t * L::kTile + c * kChunk, mq, q_full, c * (128 / L::kElem), h, tok_a + t * kBM, b);
       }
-      const int S_ = kside ? SK : SV;
-      uint64_t* full = kside ? k_full : v_full;
-      uint64_t* empty = kside ? k_empty : v_empty;
-      uint8_t* ring = kside ? sK : sV;
       int gc = 0, issued = 0;
       bool ok = true;
       for (int i = 0; ok && i < nmax; ++i) {
@@ -789,29 +776,36 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int g = t == 0 ? st.g0 : (st.shared ? -1 : st.g1);
           if (g < 0) continue;
           const int kt = t == 0 ? l0[i] : l1[i];
-          const int s = g % S_;
+          const int s = g % SK, sv = g % SV;
           const bool tt = kt >= prm.nkv;
           const int ktok = (tt ? kt - prm.nkv : kt) * kBN;
-          const CUtensorMap* map = kside ? (tt ? &tm_tk : &tm_k) : (tt ? &tm_tv : &tm_v);
-          LVSA_CLK(t_e0);
-          if (g >= S_ && !(ok = mbar_wait(&empty[s], ((g / S_) - 1) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT,
-                                          prm.wait_ns)))
+          const CUtensorMap* mk = tt ? &tm_tk : &tm_k;
+          const CUtensorMap* mv = tt ? &tm_tv : &tm_v;
+          if (g >= SK && !(ok = mbar_wait(&k_empty[s], ((g / SK) - 1) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT, prm.wait_ns)))
             break;
-          LVSA_CLK(t_e1);
-          LVSA_PROF_ADD(kside ? 8 : 9, t_e1 - t_e0);
-          if (kside) LVSA_PROF_ADD(10, 1);
-          mbar_expect_tx(&full[s], L::kTile);
+          mbar_expect_tx(&k_full[s], L::kTile);
 #pragma unroll
           for (int c = 0; c < L::kCh; ++c)
-            tma_load_4d(ring + s * L::kTile + c * kChunk, map, &full[s], c * (128 / L::kElem), hk, ktok, b);
+            tma_load_4d(sK + s * L::kTile + c * kChunk, mk, &k_full[s], c * (128 / L::kElem), hk, ktok, b);
+          if (g >= SV && !(ok = mbar_wait(&v_empty[sv], ((g / SV) - 1) & 1, abort, prm.err, LVSA_ERR_DEVICE_TIMEOUT, prm.wait_ns))) {
+            issued = -(g + 1);  // K of load g issued, V not
+            break;
+          }
+          mbar_expect_tx(&v_full[sv], L::kTile);
+#pragma unroll
+          for (int c = 0; c < L::kCh; ++c)
+            tma_load_4d(sV + sv * L::kTile + c * kChunk, mv, &v_full[sv], c * (128 / L::kElem), hk, ktok, b);
           issued = g + 1;
         }
       }
       if (*abort) {
-        // Drain this lane's own copies still in flight before the CTA retires.
-        if (kside && !skip_q) mbar_wait(q_full, 0, never, nullptr, 0);
-        for (int g = max(0, issued - S_); g < issued; ++g)
-          mbar_wait(&full[g % S_], (g / S_) & 1, never, nullptr, 0);
+        // Drain our own copies still in flight before the CTA retires.
+        const int k_issued = issued < 0 ? -issued : issued, v_issued = issued < 0 ? -issued - 1 : issued;
+        if (!skip_q) mbar_wait(q_full, 0, never, nullptr, 0);
+        for (int g = max(0, k_issued - SK); g < k_issued; ++g)
+          mbar_wait(&k_full[g % SK], (g / SK) & 1, never, nullptr, 0);
+        for (int g = max(0, v_issued - SV); g < v_issued; ++g)
+          mbar_wait(&v_full[g % SV], (g / SV) & 1, never, nullptr, 0);
       }
     }
   } else if (warp == kMmaWarp) {
