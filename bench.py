@@ -427,12 +427,14 @@ def run_e2e(args, cfg, dev, world, flop_tiles):
 
 
 def run_e2e_ulysses(args, cfg, dev, world, rank, flop_tiles, sizes, sched, local_attn):
-    """Ulysses through the public call with this rank's token shard in pinned
+    """Ulysses through the public calls with this rank's token shard in pinned
     host memory: per layer, H2D of the q/k/v (+text) shard, the head-parallel
-    layer (both all-to-alls inside), D2H of the output shard; all in the
+    layer (both all-to-alls inside), D2H of the output shard, neighbouring
+    layers' copies overlapped (``pipeline.attention_from_host``); all in the
     timed region, max over ranks."""
     import torch
     import torch.distributed as dist
+    from longvideosparseattention_b200.pipeline import attention_from_host
     from longvideosparseattention_b200.ulysses import ulysses_attention
     L, nt = cfg["layers"], cfg["n_text"]
     a0 = sum(sizes[:rank])
@@ -447,14 +449,12 @@ def run_e2e_ulysses(args, cfg, dev, world, rank, flop_tiles, sizes, sched, local
     d2h = out_h.numel() * 2 + (host[0][3].numel() * 2 if nt else 0)
     tout_h = torch.empty(host[0][3].shape, dtype=torch.bfloat16).pin_memory() if nt else None
 
+    def layer(q, k, v, tq, tk, tv):
+        return ulysses_attention(q, k, v, sizes, local_attn, tq, tk, tv, schedule=sched)
+
     def step():
-        for i in range(L):
-            d = [x.to(dev, non_blocking=True) for x in host[i & 1]]
-            tx = (d[3], d[4], d[5]) if nt else (None, None, None)
-            o, to = ulysses_attention(d[0], d[1], d[2], sizes, local_attn, *tx, schedule=sched)
-            out_h.copy_(o, non_blocking=True)
-            if nt:
-                tout_h.copy_(to, non_blocking=True)
+        ins = [tuple(host[i & 1]) if nt else tuple(host[i & 1][:3]) + (None, None, None) for i in range(L)]
+        attention_from_host(ins, None, [(out_h, tout_h)] * L, dev, layer_fn=layer)
 
     steps = max(1, min(args.steps, 2))
     step()
@@ -472,7 +472,8 @@ def run_e2e_ulysses(args, cfg, dev, world, rank, flop_tiles, sizes, sched, local
     return {"value": round(flop_tiles * L * steps / (ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
             "ms_per_layer": round(ms / steps / L, 3), "h2d_bytes_per_step": h2d * L * world,
             "d2h_bytes_per_step": d2h * L * world, "steps": steps,
-            "path": "ulysses_attention on per-rank pinned host shards (copies serialised with the layer)"}
+            "path": "ulysses_attention on per-rank pinned host shards through pipeline.attention_from_host "
+                    "(H2D of layer i+1 and D2H of layer i-1 overlap layer i)"}
 
 
 _CPU_INPUTS = {}

@@ -14,7 +14,7 @@ per layer approaches the kernel time.
 
 from __future__ import annotations
 
-from typing import List, Optional, Sequence, Tuple
+from typing import Callable, List, Optional, Sequence, Tuple
 
 import torch
 
@@ -22,12 +22,18 @@ from .block_sparse import block_sparse_attention
 
 
 def attention_from_host(inputs: Sequence[Sequence[Optional[torch.Tensor]]], mask,
-                        outputs: Sequence[Sequence[Optional[torch.Tensor]]], device: torch.device) -> None:
+                        outputs: Sequence[Sequence[Optional[torch.Tensor]]], device: torch.device,
+                        layer_fn: Optional[Callable] = None) -> None:
     """inputs[i] = (q, k, v, text_q, text_k, text_v) pinned host tensors of
     layer i (text entries None without text); outputs[i] = (out, text_out)
     pinned host tensors the results are copied into.  Runs asynchronously on
     the current stream of ``device`` (plus two copy streams); synchronize
-    that stream (or the device) before reading ``outputs``."""
+    that stream (or the device) before reading ``outputs``.
+
+    ``layer_fn(q, k, v, text_q, text_k, text_v) -> (out, text_out)``
+    replaces the single-GPU kernel call, e.g. a Ulysses layer over this
+    rank's token shard (its collectives run on the compute stream's order;
+    the copies of the neighbouring layers overlap them)."""
     n = len(inputs)
     if len(outputs) != n:
         raise ValueError("one output pair per input layer")
@@ -64,9 +70,12 @@ def attention_from_host(inputs: Sequence[Sequence[Optional[torch.Tensor]]], mask
         if i >= 2:
             compute.wait_event(copied_out[i - 2])  # out slot free
         o_slot = slots_out[i & 1]
-        o, to = block_sparse_attention(d[0], d[1], d[2], mask, d[3], d[4], d[5],
-                                       out=None if o_slot is None else o_slot[0],
-                                       text_out=None if o_slot is None else o_slot[1])
+        if layer_fn is not None:
+            o, to = layer_fn(*d)
+        else:
+            o, to = block_sparse_attention(d[0], d[1], d[2], mask, d[3], d[4], d[5],
+                                           out=None if o_slot is None else o_slot[0],
+                                           text_out=None if o_slot is None else o_slot[1])
         slots_out[i & 1] = (o, to)
         consumed[i].record(compute)
         with torch.cuda.stream(s_out):
