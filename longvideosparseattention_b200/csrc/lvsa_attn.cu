@@ -45,6 +45,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdint>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <type_traits>
@@ -78,6 +79,9 @@ constexpr uint32_t kTmemCols = 512;
 constexpr float kNegInf = -INFINITY;
 #ifndef LVSA_S3
 #define LVSA_S3 1
+#endif
+#ifndef LVSA_TEXT_FIRST
+#define LVSA_TEXT_FIRST 1
 #endif
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O only when the max grows by > 2^8
 
@@ -320,7 +324,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* never = reinterpret_cast<volatile int*>(smem + L::kMisc + 8);  // stays 0: drain waits
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int row = blockIdx.x + prm.row0, h = blockIdx.y, b = blockIdx.z;
+  // Text query rows (dense: every key tile) are the longest CTAs of a head;
+  // they take the first block indices so they start early instead of
+  // forming the launch's tail.
+  const int n_text_rows = prm.pair_end - max(prm.row0, prm.nqv);
+  const int xr = (LVSA_TEXT_FIRST && n_text_rows > 0)
+                     ? static_cast<int>((blockIdx.x + gridDim.x - n_text_rows) % gridDim.x)
+                     : static_cast<int>(blockIdx.x);
+  const int row = xr + prm.row0, h = blockIdx.y, b = blockIdx.z;
   const int beg = prm.indptr[row];
   const int n = prm.indptr[row + 1] - beg;
   const bool text_row = row >= prm.nqv;
@@ -711,7 +722,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   LVSA_CLK(t_cta0);
   const int h = blockIdx.y, b = blockIdx.z;
   // Pairs of video rows [row0, pair_ve), then pairs of text rows [pair_ts, pair_end).
-  const int x = blockIdx.x;
+  // Text pairs (dense rows, the longest CTAs) take the first block indices.
+  const int x = (LVSA_TEXT_FIRST && static_cast<int>(gridDim.x) > prm.pair_nv)
+                    ? static_cast<int>((blockIdx.x + prm.pair_nv) % gridDim.x)
+                    : static_cast<int>(blockIdx.x);
   const bool text_row = x >= prm.pair_nv;
   const int row_a = text_row ? prm.pair_ts + 2 * (x - prm.pair_nv) : prm.row0 + 2 * x;
   const bool has_b = row_a + 1 < (text_row ? prm.pair_end : prm.pair_ve);
@@ -1190,6 +1204,33 @@ int validate(const LvsaAttnArgs* a) {
 }
 }  // namespace
 
+// bf16/f16 at D = 128: the tile-pair kernel (two query tiles per CTA share
+// their K/V loads) when its grid holds at least LVSA_PAIR_MIN_WAVES waves of
+// CTAs, else the single-tile kernel, whose CTAs are half as long and so
+// leave half the last-wave tail.  Measured (ms per launch): cfg2, 12 heads,
+// 40 waves: pair 32.25 vs single 32.61; cfg4 with 2 heads (one rank's share
+// on 8 GPUs), 4.1 waves: pair 2.52 vs single 2.30.  LVSA_ATTN_KERNEL=pair /
+// single in the environment forces one (tests).
+#ifndef LVSA_PAIR_MIN_WAVES
+#define LVSA_PAIR_MIN_WAVES 16
+#endif
+bool use_pair_kernel(const LvsaAttnArgs* a) {
+  if (const char* e = std::getenv("LVSA_ATTN_KERNEL")) {
+    if (!std::strcmp(e, "pair")) return true;
+    if (!std::strcmp(e, "single")) return false;
+  }
+  const bool text_rows = a->n_text > 0 && a->text_q.ptr != nullptr;
+  const int end = std::min(text_rows ? a->n_q_tiles : a->n_q_video_tiles,
+                           a->end_q_tile > 0 ? a->end_q_tile : a->n_q_tiles);
+  const int first = a->first_q_tile, nqv = a->n_q_video_tiles;
+  const int ve = std::min(end, nqv), ts = std::max(first, nqv);
+  const long long pairs = (ve > first ? (ve - first + 1) / 2 : 0) + (end > ts ? (end - ts + 1) / 2 : 0);
+  const long long ctas = pairs * a->heads * a->batch;
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return ctas >= static_cast<long long>(LVSA_PAIR_MIN_WAVES) * sms;
+}
+
 // The argument and geometry checks of lvsa_attn_fwd / lvsa_attn_fwd_fp8, for
 // entry points that must reject a call before they launch anything.
 int validate_attn_args(const LvsaAttnArgs* a) { return validate(a); }
@@ -1228,8 +1269,11 @@ extern "C" int lvsa_attn_fwd(const LvsaAttnArgs* a, void* stream) {
 #define LVSA_SVP 2
 #endif
 #if LVSA_PAIR
-    case 128: return bf16 ? launch<128, LVSA_SKP, LVSA_SVP, true, false, true>(a, s)
-                          : launch<128, LVSA_SKP, LVSA_SVP, false, false, true>(a, s);
+    case 128:
+      if (use_pair_kernel(a))
+        return bf16 ? launch<128, LVSA_SKP, LVSA_SVP, true, false, true>(a, s)
+                    : launch<128, LVSA_SKP, LVSA_SVP, false, false, true>(a, s);
+      return bf16 ? launch<128, LVSA_SK, LVSA_SV, true>(a, s) : launch<128, LVSA_SK, LVSA_SV, false>(a, s);
 #else
     case 128: return bf16 ? launch<128, LVSA_SK, LVSA_SV, true>(a, s) : launch<128, LVSA_SK, LVSA_SV, false>(a, s);
 #endif

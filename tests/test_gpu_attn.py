@@ -185,12 +185,16 @@ def test_attention_baseline_configs_sampled(cfg):
         assert (t1.float() - 1).abs().max().item() <= 1e-2
 
 
-@pytest.mark.parametrize("D,fp8", [(128, False), (64, False), (128, True)])
-def test_attention_arbitrary_tile_lists(D, fp8):
+@pytest.mark.parametrize("D,fp8,kernel", [(128, False, "pair"), (128, False, "single"), (64, False, "auto"),
+                                          (128, True, "auto")])
+def test_attention_arbitrary_tile_lists(D, fp8, kernel, monkeypatch):
     """Hand-made tile CSR (no in-tile masks): adjacent query tiles with equal,
     nested, disjoint, reordered and empty key-tile lists, and an odd number of
     query tiles.  Exercises every branch of the tile-pair kernel's shared load
-    sequence (bf16 D=128) and the single-tile kernel (D=64, FP8)."""
+    sequence (bf16 D=128, forced: this grid is below the pair kernel's
+    launch threshold) and the single-tile kernel (bf16 D=128 forced, D=64,
+    FP8)."""
+    monkeypatch.setenv("LVSA_ATTN_KERNEL", kernel)
     import dataclasses
     from longvideosparseattention_b200 import block_sparse_attention, build_block_mask, check_device_errors
     T, P, H, B = 9, 128, 2, 1          # 9 query tiles of 128 tokens, 9 key tiles

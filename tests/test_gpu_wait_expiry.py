@@ -15,8 +15,10 @@ from tests.gpu_util import assert_close, seeded, to_np
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("D,fp8", [(128, False), (64, False), (128, True)])
-def test_expired_wait_reports_timeout_and_context_survives(D, fp8):
+@pytest.mark.parametrize("D,fp8,kernel", [(128, False, "pair"), (128, False, "single"), (64, False, "auto"),
+                                          (128, True, "auto")])
+def test_expired_wait_reports_timeout_and_context_survives(D, fp8, kernel, monkeypatch):
+    monkeypatch.setenv("LVSA_ATTN_KERNEL", kernel)
     from longvideosparseattention_b200 import _native as N
     from longvideosparseattention_b200 import block_sparse_attention, build_block_mask, check_device_errors
     dev = torch.device("cuda")
